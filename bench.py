@@ -1,0 +1,418 @@
+"""Benchmark of the localcorr hot path (RAFT pyramid correlation, fwd+bwd).
+
+Contract: ``python bench.py --gpus N --steps K --warmup W [--impl ours|reference]``
+prints ONE JSON line on rank 0. Under torchrun (N>1) every rank runs the
+same per-GPU workload on its own batch shard with no collective in the data
+path (weak scaling); the timed region is bracketed by a barrier and a device
+synchronisation on both sides and the elapsed time is the max over ranks.
+
+Workload (default, benchmark configuration 2): RAFT 1/8-resolution training
+correlation, float16, B=8 per GPU, C=256, 135x240, 4 levels, radius 4.
+fmap1/fmap2 ~ N(0,1) (the 1/sqrt(C) is the block's output scale), coords =
+grid + N(0, 6^2) flow with 5% of the pixels pushed out of bounds, 12 lookups
+per step with coords perturbed by N(0,1) each. One step = block build (NHWC
+transpose + pyramid) + 12 x (forward + backward) + the pyramid/transpose
+backward, through the public API (get_localcorr_block + autograd).
+Metric: lookups = B*H*W*L*(2r+1)^2 per lookup call; value = Glookups/s of
+the whole job. Inputs (265 MB of maps + 2 GB of upstream gradients per GPU)
+are larger than L2, so no explicit flush is needed between steps.
+
+The reference arm (--impl reference) times the reference's CPU path as
+restated in oracle/oracle.py (the all-pairs matmul + grid_sample formulation
+of onnx_generic.py:58-156) on the host cores, on a bounded sample.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+import torch  # noqa: E402
+
+CONFIGS = {
+    # name: (B per GPU, C, H, W, levels, radius, lookups per step, dtype)
+    "raft_train_1080p": dict(B=8, C=256, H=135, W=240, L=4, r=4, iters=12, dtype="f16",
+                             coords="gauss_oob", fdist="normal", backward=True),
+    "raft_cpu_case": dict(B=1, C=256, H=46, W=62, L=4, r=4, iters=1, dtype="f32",
+                          coords="uniform8", fdist="normal", backward=True),
+    "raft_4k_inference": dict(B=1, C=256, H=270, W=480, L=4, r=4, iters=24, dtype="f16",
+                              coords="smooth", fdist="normal", backward=False),
+    "highbatch_r3": dict(B=8, C=128, H=64, W=128, L=4, r=3, iters=1, dtype="f16",
+                         coords="uniform64", fdist="uniform", backward=True),
+    "highbatch_r4": dict(B=8, C=128, H=64, W=128, L=4, r=4, iters=1, dtype="f16",
+                         coords="uniform64", fdist="uniform", backward=True),
+    "highbatch_r8": dict(B=8, C=128, H=64, W=128, L=4, r=8, iters=1, dtype="f16",
+                         coords="uniform64", fdist="uniform", backward=True),
+}
+DEFAULT = "raft_train_1080p"
+METRIC = "corr Glookups/s fwd+bwd (B*H*W*L*(2r+1)^2)"
+
+
+def _env_rank():
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)),
+            int(os.environ.get("WORLD_SIZE", 1)))
+
+
+def _peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d.get("hbm_gbs", 6650.0)), "measured"
+    return 6650.0, "fallback"
+
+
+def lookups_per_call(cfg):
+    return cfg["B"] * cfg["H"] * cfg["W"] * cfg["L"] * (2 * cfg["r"] + 1) ** 2
+
+
+def algorithmic_bytes(cfg, kernel):
+    """Bytes each tensor of one engine call occupies, touched once (storage dtype)."""
+    es = 2 if cfg["dtype"] == "f16" else 4
+    b, c, h, w, L, r = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["L"], cfg["r"]
+    p = b * h * w
+    pyr = sum(b * (h >> l) * (w >> l) * c for l in range(L)) * es
+    f1 = p * c * es
+    coords = 2 * p * es
+    out = p * L * (2 * r + 1) ** 2 * es
+    fwd = f1 + pyr + coords + out
+    if kernel == "pyramid_fwd":
+        return fwd
+    # backward: reads f1, pyramid, coords, corr_grad; writes grad_f1 and the
+    # float32 grad pyramid (the C ABI's accumulator).
+    return fwd + f1 + pyr * (4 // es)
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self._thr = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self._thr = threading.Thread(target=self._read, daemon=True)
+        self._thr.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self._thr:
+            self._thr.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() in ("active", "1", "yes"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_inputs(cfg, rank, device):
+    from oracle import oracle
+
+    g = torch.Generator().manual_seed(1234 + rank)
+    dt = torch.float16 if cfg["dtype"] == "f16" else torch.float32
+    b, c, h, w = cfg["B"], cfg["C"], cfg["H"], cfg["W"]
+    f1, f2 = oracle.make_fmaps(b, c, h, w, seed=1234 + rank, dist=cfg["fdist"])
+    kind = cfg["coords"]
+    if kind == "gauss_oob":
+        c0 = oracle.make_coords_gauss_oob(b, h, w, 6.0, 0.05, seed=99 + rank)
+    elif kind == "smooth":
+        c0 = oracle.make_coords_smooth(b, h, w, 40.0, seed=99 + rank)
+    elif kind == "uniform64":
+        c0 = oracle.make_coords_uniform(b, h, w, 64.0, seed=99 + rank)
+    else:
+        c0 = oracle.make_coords_uniform(b, h, w, 8.0, seed=99 + rank)
+    coords = []
+    for i in range(cfg["iters"]):
+        if i == 0:
+            coords.append(c0)
+        else:
+            coords.append(coords[-1] + torch.randn(c0.shape, generator=g))
+    rd = 2 * cfg["r"] + 1
+    grads = None
+    if cfg["backward"]:
+        grads = [torch.randn(b, cfg["L"] * rd * rd, h, w, generator=g).to(dt)
+                 for _ in range(cfg["iters"])]
+    host = dict(
+        f1=f1.to(dt).pin_memory(), f2=f2.to(dt).pin_memory(),
+        coords=[co.to(dt).pin_memory() for co in coords],
+    )
+    dev = dict(
+        f1=host["f1"].to(device), f2=host["f2"].to(device),
+        coords=[co.to(device) for co in host["coords"]],
+        grads=[gg.to(device) for gg in grads] if grads is not None else None,
+    )
+    return host, dev
+
+
+def run_step(cfg, f1, f2, coords, grads):
+    import localcorr_b200 as lc
+
+    if cfg["backward"]:
+        f1 = f1.detach().requires_grad_(True)
+        f2 = f2.detach().requires_grad_(True)
+        block = lc.get_localcorr_block(f1, f2, num_levels=cfg["L"], radius=cfg["r"],
+                                       corr_mode="localcorr_cuda")
+        outs = [block(co) for co in coords]
+        torch.autograd.backward(outs, grads)
+        return f1.grad, f2.grad
+    with torch.no_grad():
+        block = lc.get_localcorr_block(f1, f2, num_levels=cfg["L"], radius=cfg["r"],
+                                       corr_mode="localcorr_cuda")
+        outs = [block(co) for co in coords]
+    return outs[-1], None
+
+
+def timed_loop(fn, steps, device):
+    torch.cuda.synchronize(device)
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        fn()
+    end.record()
+    torch.cuda.synchronize(device)
+    return start.elapsed_time(end) / 1e3
+
+
+def cpu_baseline_sample(cfg, seconds_hint=20.0):
+    """Time the reference CPU formulation (restated in oracle/oracle.py) on a
+    bounded sample: one image, a band of fmap1 rows, fwd + bwd, float32."""
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    c, h, w, L, r = cfg["C"], cfg["H"], cfg["W"], cfg["L"], cfg["r"]
+    rows = max(1, min(h, 32))
+    f1, f2 = oracle.make_fmaps(1, c, h, w, seed=5)
+    co = oracle.make_coords_gauss_oob(1, h, w, 6.0, 0.05, seed=6)
+    f1 = f1[:, :, :rows].contiguous().requires_grad_(True)
+    f2 = f2.clone().requires_grad_(True)
+    co = co[:, :, :rows].contiguous()
+    t0 = time.perf_counter()
+    out = oracle.pyramid_corr_matmul(f1, f2, co, L, r) / math.sqrt(c)
+    out.backward(torch.ones_like(out))
+    dt = time.perf_counter() - t0
+    n = rows * w * L * (2 * r + 1) ** 2
+    return {"value": n / dt / 1e9, "unit": "Glookups/s", "cores": threads, "kind": "port",
+            "sample": f"1 image, {rows} of {h} fmap1 rows x {w} cols, C={c}, L={L}, r={r}, "
+                      "fp32, fwd+bwd, oracle/oracle.py:pyramid_corr_matmul",
+            "seconds": dt}
+
+
+def reference_arm(args, cfg, cfg_name):
+    rank, _, world = _env_rank()
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    for _ in range(args.warmup):
+        cpu_baseline_sample(cfg)
+    vals = []
+    t_total = 0.0
+    for _ in range(args.steps):
+        s = cpu_baseline_sample(cfg)
+        vals.append(s["value"])
+        t_total += s["seconds"]
+    v = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": v, "unit": "Glookups/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t_total / max(1, args.steps), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg_name, "per_step": s["sample"]},
+        "cpu_baseline": {k: s[k] for k in ("unit", "cores", "kind", "sample")} | {"value": v},
+        "e2e": {"value": v, "unit": "Glookups/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", default=DEFAULT, choices=sorted(CONFIGS))
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args(argv)
+    cfg = dict(CONFIGS[args.config])
+    if args.impl == "reference":
+        return reference_arm(args, cfg, args.config)
+
+    rank, local_rank, world = _env_rank()
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=device)
+    from localcorr_b200 import _lib, ops
+
+    lib = _lib.require_library()
+    host, dev = make_inputs(cfg, rank, device)
+
+    def step():
+        return run_step(cfg, dev["f1"], dev["f2"], dev["coords"], dev["grads"])
+
+    for _ in range(max(3, args.warmup)):
+        step()
+    torch.cuda.synchronize(device)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier()
+
+    # ---- timed region: device-resident inputs ----
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+    records = []
+    ops.set_launch_timer(records)
+    lib.localCorrB200LaunchCount(1)
+    barrier()
+    elapsed = timed_loop(step, args.steps, device)
+    barrier()
+    launches = int(lib.localCorrB200LaunchCount(1))
+    ops.set_launch_timer(None)
+    clocks = sampler.stop() if sampler else None
+    if dist is not None:
+        t = torch.tensor([elapsed], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed = float(t.item())
+        n = torch.tensor([launches], device=device, dtype=torch.float64)
+        dist.all_reduce(n)
+        launches = int(n.item())
+
+    # per-kernel durations from the live events
+    per = {}
+    for name, s, e in records:
+        per.setdefault(name, []).append(s.elapsed_time(e) / 1e3)
+    kern = max(per, key=lambda k: sum(per[k])) if per else None
+
+    # ---- end-to-end through the public API with host buffers ----
+    def e2e_step():
+        f1 = host["f1"].to(device, non_blocking=True)
+        f2 = host["f2"].to(device, non_blocking=True)
+        coords = [co.to(device, non_blocking=True) for co in host["coords"]]
+        g1, g2 = run_step(cfg, f1, f2, coords, dev["grads"])
+        chk = g1.float().sum() + (g2.float().sum() if g2 is not None else 0.0)
+        return chk.item()
+
+    for _ in range(2):
+        e2e_step()
+    barrier()
+    e2e_elapsed = timed_loop(e2e_step, args.steps, device)
+    barrier()
+    if dist is not None:
+        t = torch.tensor([e2e_elapsed], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_elapsed = float(t.item())
+
+    lookups_step = lookups_per_call(cfg) * cfg["iters"]
+    value = lookups_step * args.steps * world / elapsed / 1e9
+    e2e_value = lookups_step * args.steps * world / e2e_elapsed / 1e9
+    h2d = (host["f1"].numel() + host["f2"].numel()) * host["f1"].element_size() + sum(
+        co.numel() * co.element_size() for co in host["coords"])
+
+    line = None
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        roof = None
+        if kern:
+            dur = statistics.mean(per[kern])
+            abytes = algorithmic_bytes(cfg, kern)
+            achieved = abytes / dur / 1e9
+            traffic = None
+            tf = ROOT / "profiles" / "traffic.json"
+            if tf.exists():
+                traffic = json.loads(tf.read_text()).get(f"{args.config}:{kern}")
+            roof = {"bound": "hbm", "kernel": kern, "achieved": achieved, "peak": peak,
+                    "peak_source": peak_kind, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": traffic, "algorithmic_bytes": abytes,
+                    "launch_ms": 1e3 * dur, "launches_timed": len(per[kern]),
+                    "share_of_step": sum(per[kern]) / elapsed,
+                    "per_kernel_ms": {k: 1e3 * statistics.mean(v) for k, v in per.items()}}
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_baseline_sample(cfg)
+            cpu.pop("seconds", None)
+        line = {
+            "metric": METRIC, "value": value, "unit": "Glookups/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup),
+            "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None,
+            "dtype": cfg["dtype"], "data": "synthetic",
+            "config": {"workload": args.config, "B_per_gpu": cfg["B"], "global_batch":
+                       cfg["B"] * world, "C": cfg["C"], "H": cfg["H"], "W": cfg["W"],
+                       "levels": cfg["L"], "radius": cfg["r"], "lookups_per_step":
+                       cfg["iters"], "backward": cfg["backward"],
+                       "parallelism": f"batch-shard x{world}, no collective",
+                       "l2": "inputs larger than L2 (no flush)"},
+            "e2e": {"value": e2e_value, "unit": "Glookups/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": 4},
+            "gpu_launches": launches,
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "clocks": clocks,
+        }
+        print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,169 @@
+/*
+ * localcorr_b200 — C ABI of the B200 (sm_100a) local-correlation library
+ * (liblocalcorr_b200.so).
+ *
+ * Tensor contract shared by every pyramid entry point (identical to the
+ * contract of the reference library's launchers):
+ *   fmap1        [B, H1, W1, C]           contiguous, NHWC
+ *   fmap2_packed [B, C * sum_l h_l * w_l] contiguous, batch-major; level l of
+ *                batch b starts at b*P + C*sum_{j<l} h_j*w_j and is NHWC;
+ *                h_l = H1 >> l, w_l = W1 >> l
+ *   coords       [B, 2, H1, W1]           contiguous, planar (x, then y),
+ *                                         level-0 pixel units
+ *   corr         [B, levels, RD*RD, H1, W1], RD = 2*radius+1
+ *   corr[b,l,d,h,w] = sum_c fmap1[b,h,w,c] *
+ *        bilinear(fmap2_l[b], coords[b,:,h,w]/2^l + dilation*(ix-r, iy-r))[c]
+ *   with zero padding outside fmap2_l, d = iy + RD*ix (ymajor=false, RAFT
+ *   order) or d = ix + RD*iy (ymajor=true, spatial-sampler order).
+ *
+ * All launchers are asynchronous on `stream`, never synchronise the host and
+ * return true on success (or for an empty problem: B <= 0 or H1*W1 <= 0) and
+ * false for an invalid configuration or a launch error; the reason is then
+ * available from localCorrB200GetLastError() (thread-local).
+ *
+ * dtype codes: LCB200_F32 = 0 (float32), LCB200_F16 = 1 (float16).
+ */
+#ifndef LOCALCORR_B200_H
+#define LOCALCORR_B200_H
+
+#include <stddef.h>
+#include <stdbool.h>
+#include <cuda_runtime.h>
+
+#if defined(__GNUC__)
+#define LCB200_API __attribute__((visibility("default")))
+#else
+#define LCB200_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LCB200_F32 0
+#define LCB200_F16 1
+
+/* Engine selection for the extended pyramid launchers. */
+#define LCB200_ENGINE_AUTO 0    /* tensor-core engine when eligible, else CUDA-core */
+#define LCB200_ENGINE_SIMT 1    /* CUDA-core engine, every configuration */
+#define LCB200_ENGINE_TC 2      /* tensor-core engine; fails if not eligible */
+
+/* ---- Reference-compatible entry points ------------------------------------
+ * Same symbol names, argument order, argument meaning and error behaviour as
+ * the reference library, so its ctypes loader (blocks.py:74-131) and its
+ * TensorRT plugin enqueue (cuda_pyramid/localcorr_cuda_pyramid_plugin.cpp:
+ * 164-199) bind to this library unchanged.
+ */
+
+/* Replaces launchLocalCorrCudaPyramidForward,
+ * cuda_pyramid/localcorr_cuda_pyramid_kernel.h:39-53. isHalf selects float16
+ * for every pointer. Scratch, when the tensor-core engine needs it, comes from
+ * a per-device cache owned by the library (stream-ordered, grown on demand). */
+LCB200_API bool launchLocalCorrCudaPyramidForward(
+    const void* fmap1, const void* fmap2_packed, const void* coords, void* corr,
+    int B, int H1, int W1, int C, int radius, int levels, int dilation,
+    bool isHalf, bool ymajor, cudaStream_t stream);
+
+/* Replaces launchLocalCorrCudaPyramidBackward,
+ * cuda_pyramid/localcorr_cuda_pyramid_kernel.h:82-98. fmap1_grad is written
+ * in the input dtype; fmap2_grad must be a zero-initialised float32 buffer
+ * with fmap2_packed's element count and receives the fmap2 gradient
+ * (accumulated, so several calls may share it). coords get no gradient. */
+LCB200_API bool launchLocalCorrCudaPyramidBackward(
+    const void* fmap1, const void* fmap2_packed, const void* coords,
+    const void* corr_grad, void* fmap1_grad, float* fmap2_grad,
+    int B, int H1, int W1, int C, int radius, int levels, int dilation,
+    bool isHalf, bool ymajor, cudaStream_t stream);
+
+/* ---- Extended pyramid entry points (no reference counterpart beyond the
+ * launchers above: they add an output scale, an engine choice and a
+ * caller-provided workspace) ------------------------------------------------ */
+
+/* Bytes of workspace the pyramid forward/backward need for this shape and
+ * engine (0 when the engine needs none). */
+LCB200_API size_t localCorrB200PyramidWorkspaceBytes(
+    int B, int H1, int W1, int C, int radius, int levels, int dilation,
+    int dtype, int engine);
+
+/* corr = scale * (the reference forward). The 1/sqrt(C) of the RAFT block
+ * (blocks.py:411) is passed as scale instead of a separate division pass.
+ * coords_dtype may differ from dtype (float32 coords with float16 maps keep
+ * sub-pixel precision at large coordinates).
+ * workspace may be NULL when localCorrB200PyramidWorkspaceBytes() is 0;
+ * otherwise it must hold at least that many bytes (256-byte aligned). */
+LCB200_API bool launchLocalCorrB200PyramidForward(
+    const void* fmap1, const void* fmap2_packed, const void* coords, void* corr,
+    int B, int H1, int W1, int C, int radius, int levels, int dilation,
+    int dtype, int coords_dtype, bool ymajor, float scale, int engine,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* Backward of launchLocalCorrB200PyramidForward (gradient of the scaled
+ * output). fmap1_grad (dtype) is overwritten. fmap2_grad_f32 (float32,
+ * fmap2_packed's element count) is accumulated into when accumulate is true
+ * and overwritten otherwise. */
+LCB200_API bool launchLocalCorrB200PyramidBackward(
+    const void* fmap1, const void* fmap2_packed, const void* coords,
+    const void* corr_grad, void* fmap1_grad, float* fmap2_grad_f32,
+    int B, int H1, int W1, int C, int radius, int levels, int dilation,
+    int dtype, int coords_dtype, bool ymajor, float scale, bool accumulate, int engine,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
+/* ---- Layout preparation (replaces the torch permute/avg_pool2d/cat chain of
+ * LocalCorrCudaPyramidBlock.__init__, blocks.py:369-383) ------------------- */
+
+/* fmap2 [B,C,H,W] (NCHW) -> fmap2_packed (layout above), levels built by 2x2
+ * average pooling with floor-halved dims, each level pooled from the previous
+ * level's dtype-rounded values as torch's avg_pool2d chain does. */
+LCB200_API bool launchLocalCorrB200PyramidBuild(
+    const void* fmap2_nchw, void* fmap2_packed,
+    int B, int C, int H, int W, int levels, int dtype, cudaStream_t stream);
+
+/* Gradient of launchLocalCorrB200PyramidBuild: grad_packed (float32 when
+ * grad_is_f32, else dtype) -> grad_fmap2_nchw (dtype, overwritten). */
+LCB200_API bool launchLocalCorrB200PyramidBuildBackward(
+    const void* grad_packed, bool grad_is_f32, void* grad_fmap2_nchw,
+    int B, int C, int H, int W, int levels, int dtype, cudaStream_t stream);
+
+/* [B, C, HW] <-> [B, HW, C] layout transposes (fmap1 NCHW <-> NHWC). */
+LCB200_API bool launchLocalCorrB200NchwToNhwc(const void* in, void* out, int B, int C,
+                                   int HW, int dtype, cudaStream_t stream);
+LCB200_API bool launchLocalCorrB200NhwcToNchw(const void* in, void* out, int B, int C,
+                                   int HW, int dtype, cudaStream_t stream);
+
+/* ---- Spatial (PWC-Net) correlation ---------------------------------------
+ * Replaces the sampler path LocalCorrCudaSpatialSampler (blocks.py:671-694)
+ * / LocalCorrCudaPyramidSampler (spatial_corr.py:328-376), which runs the
+ * pyramid launcher with levels=1, ymajor and identity coords:
+ *   out[b, iy, ix, h, w] = scale * sum_c in1[b,c,h,w] *
+ *                          in2[b, c, h + dil*(iy-r), w + dil*(ix-r)]
+ * (zero outside), in1/in2 [B,C,H,W] NCHW, out [B, RD, RD, H, W]. */
+LCB200_API bool launchLocalCorrB200SpatialForward(
+    const void* in1, const void* in2, void* out,
+    int B, int C, int H, int W, int radius, int dilation, int dtype,
+    float scale, cudaStream_t stream);
+
+/* Gradients of the spatial correlation; grad_in1/grad_in2 (dtype, NCHW) are
+ * overwritten. Either may be NULL to skip it. */
+LCB200_API bool launchLocalCorrB200SpatialBackward(
+    const void* in1, const void* in2, const void* grad_out,
+    void* grad_in1, void* grad_in2,
+    int B, int C, int H, int W, int radius, int dilation, int dtype,
+    float scale, cudaStream_t stream);
+
+/* ---- Diagnostics ---------------------------------------------------------- */
+
+/* Message of the last failed call on this thread ("" if none). */
+LCB200_API const char* localCorrB200GetLastError(void);
+
+/* Library ABI version (major*10000 + minor*100 + patch). */
+LCB200_API int localCorrB200Version(void);
+
+/* Number of kernel launches issued by this library on this thread since the
+ * last reset (diagnostics for launch accounting in benchmarks). */
+LCB200_API long long localCorrB200LaunchCount(int reset);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LOCALCORR_B200_H */

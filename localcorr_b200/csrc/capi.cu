@@ -1,0 +1,399 @@
+// extern "C" entry points of liblocalcorr_b200.so (declared in
+// include/localcorr_b200.h): argument validation, engine selection and
+// error reporting around the kernels.
+#include <atomic>
+#include <mutex>
+#include <string>
+
+#include "lc_common.cuh"
+
+namespace lcb200 {
+
+// Engines (defined in corr_simt.cu, corr_tc.cu, layout.cu, spatial.cu).
+bool simt_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
+                  int, int, int, bool, float, cudaStream_t);
+bool simt_backward(const void*, const void*, const void*, const void*, void*, float*, int,
+                   int, int, int, int, int, int, int, int, bool, float, cudaStream_t);
+bool tc_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
+                 int dtype, std::string* why);
+size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels);
+bool tc_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
+                int, bool, float, void*, size_t, cudaStream_t);
+bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int, int,
+                 int, int, int, int, int, bool, float, void*, size_t, cudaStream_t);
+bool layout_nchw_to_nhwc(const void*, void*, int, int, int, int, cudaStream_t);
+bool layout_nhwc_to_nchw(const void*, void*, int, int, int, int, cudaStream_t);
+bool layout_pyramid_build(const void*, void*, int, int, int, int, int, int, cudaStream_t);
+bool layout_pyramid_build_grad(const void*, bool, void*, int, int, int, int, int, int,
+                               cudaStream_t);
+bool spatial_forward(const void*, const void*, void*, int, int, int, int, int, int, int, float,
+                     cudaStream_t);
+bool spatial_backward(const void*, const void*, const void*, void*, void*, int, int, int, int,
+                      int, int, int, float, cudaStream_t);
+
+namespace {
+thread_local std::string g_last_error;
+thread_local long long g_launches = 0;
+}  // namespace
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+void clear_error() { g_last_error.clear(); }
+void count_launch(int n) { g_launches += n; }
+
+bool check_launch(const char* what) {
+  const cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) return true;
+  set_error(std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")");
+  return false;
+}
+
+int max_dyn_smem() {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int v = 0;
+  if (cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess)
+    v = 48 * 1024;
+  return v;
+}
+
+bool ensure_smem_attr(const void* func, size_t bytes) {
+  if (bytes <= 48 * 1024) return true;
+  // (kernel, device) -> largest size already granted. Small fixed table: the
+  // library has a bounded number of kernels that opt in.
+  struct Entry { const void* f; int dev; size_t bytes; };
+  static Entry table[256];
+  static int n = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < n; ++i)
+    if (table[i].f == func && table[i].dev == dev && table[i].bytes >= bytes) return true;
+  const cudaError_t e =
+      cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+  if (e != cudaSuccess) {
+    set_error(std::string("cudaFuncSetAttribute(MaxDynamicSharedMemorySize=") +
+              std::to_string(bytes) + "): " + cudaGetErrorString(e));
+    return false;
+  }
+  for (int i = 0; i < n; ++i)
+    if (table[i].f == func && table[i].dev == dev) { table[i].bytes = bytes; return true; }
+  if (n < 256) table[n++] = Entry{func, dev, bytes};
+  return true;
+}
+
+namespace {
+
+// Validation shared by all pyramid launchers, mirroring the reference
+// launchers (cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:1420-1435) plus the
+// checks the reference leaves implicit (non-negative radius, positive C,
+// 32-bit index ranges).
+bool validate_pyramid(int B, int H1, int W1, int C, int radius, int levels, int dilation,
+                      int dtype, bool* empty) {
+  *empty = false;
+  if ((long long)H1 * W1 <= 0 || B <= 0) { *empty = true; return true; }
+  if (levels < 1 || levels > kMaxLevels) {
+    set_error("levels must be in [1, 8] (got " + std::to_string(levels) + ")");
+    return false;
+  }
+  if (dilation < 1) {
+    set_error("dilation must be >= 1 (got " + std::to_string(dilation) + ")");
+    return false;
+  }
+  if (radius < 0) {
+    set_error("radius must be >= 0 (got " + std::to_string(radius) + ")");
+    return false;
+  }
+  if (C <= 0) {
+    set_error("C must be positive (got " + std::to_string(C) + ")");
+    return false;
+  }
+  if (dtype != LCB200_F32 && dtype != LCB200_F16) {
+    set_error("dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
+    return false;
+  }
+  for (int l = 0; l < levels; ++l) {
+    if ((H1 >> l) < 1 || (W1 >> l) < 1) {
+      set_error("level " + std::to_string(l) + " of a " + std::to_string(H1) + "x" +
+                std::to_string(W1) + " map is empty");
+      return false;
+    }
+  }
+  if ((long long)H1 * W1 > (1ll << 30)) {
+    set_error("H1*W1 too large");
+    return false;
+  }
+  return true;
+}
+
+// Library-owned scratch for the reference-compatible launchers, which take no
+// workspace argument. One buffer per device, grown with stream-ordered
+// cudaMallocAsync; the previous buffer is released with cudaFreeAsync on the
+// same stream, so no host synchronisation is needed.
+struct DeviceScratch {
+  void* ptr = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_scratch_mu;
+DeviceScratch g_scratch[64];
+
+void* library_scratch(size_t bytes, cudaStream_t s) {
+  if (bytes == 0) return nullptr;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  DeviceScratch& d = g_scratch[dev];
+  if (d.bytes >= bytes) return d.ptr;
+  if (d.ptr) cudaFreeAsync(d.ptr, s);
+  d.ptr = nullptr;
+  d.bytes = 0;
+  void* p = nullptr;
+  if (cudaMallocAsync(&p, bytes, s) != cudaSuccess) {
+    cudaGetLastError();
+    set_error("could not allocate " + std::to_string(bytes) + " B of scratch");
+    return nullptr;
+  }
+  d.ptr = p;
+  d.bytes = bytes;
+  return p;
+}
+
+bool use_tc(int engine, int B, int H1, int W1, int C, int radius, int levels, int dilation,
+            int dtype, bool* ok) {
+  *ok = true;
+  if (engine == LCB200_ENGINE_SIMT) return false;
+  std::string why;
+  const bool elig = tc_eligible(B, H1, W1, C, radius, levels, dilation, dtype, &why);
+  if (engine == LCB200_ENGINE_TC && !elig) {
+    set_error("tensor-core engine not eligible: " + why);
+    *ok = false;
+    return false;
+  }
+  if (engine != LCB200_ENGINE_AUTO && engine != LCB200_ENGINE_TC) {
+    set_error("unknown engine " + std::to_string(engine));
+    *ok = false;
+    return false;
+  }
+  return elig;
+}
+
+bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1,
+                     int W1, int C, int radius, int levels, int dil, int dtype, int cdtype,
+                     bool ymajor, float scale, int engine, void* ws, size_t ws_bytes,
+                     bool lib_ws, cudaStream_t s) {
+  clear_error();
+  bool empty = false;
+  if (!validate_pyramid(B, H1, W1, C, radius, levels, dil, dtype, &empty)) return false;
+  if (empty) return true;
+  if (cdtype != LCB200_F32 && cdtype != LCB200_F16) {
+    set_error("coords dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
+    return false;
+  }
+  bool ok = true;
+  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok)) {
+    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
+    if (lib_ws) {
+      ws = library_scratch(need, s);
+      ws_bytes = ws ? need : 0;
+      if (!ws && need) return false;
+    } else if (ws_bytes < need || (need && ws == nullptr)) {
+      set_error("workspace too small: need " + std::to_string(need) + " B, got " +
+                std::to_string(ws_bytes));
+      return false;
+    }
+    return tc_forward(f1, f2, co, out, B, H1, W1, C, radius, levels, cdtype, ymajor, scale, ws,
+                      ws_bytes, s);
+  }
+  if (!ok) return false;
+  return simt_forward(f1, f2, co, out, B, H1, W1, C, radius, levels, dil, dtype, cdtype, ymajor,
+                      scale, s);
+}
+
+bool pyramid_backward(const void* f1, const void* f2, const void* co, const void* gout,
+                      void* f1g, float* f2g, int B, int H1, int W1, int C, int radius,
+                      int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
+                      bool accumulate, int engine, void* ws, size_t ws_bytes, bool lib_ws,
+                      cudaStream_t s) {
+  clear_error();
+  bool empty = false;
+  if (!validate_pyramid(B, H1, W1, C, radius, levels, dil, dtype, &empty)) return false;
+  if (empty) return true;
+  if (cdtype != LCB200_F32 && cdtype != LCB200_F16) {
+    set_error("coords dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
+    return false;
+  }
+  if (!accumulate) {
+    const PyrGeom g = make_geom(H1, W1, C, levels);
+    if (cudaMemsetAsync(f2g, 0, sizeof(float) * (size_t)B * g.batch_elems, s) != cudaSuccess)
+      return check_launch("memset fmap2_grad");
+  }
+  bool ok = true;
+  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok)) {
+    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
+    if (lib_ws) {
+      ws = library_scratch(need, s);
+      ws_bytes = ws ? need : 0;
+      if (!ws && need) return false;
+    } else if (ws_bytes < need || (need && ws == nullptr)) {
+      set_error("workspace too small: need " + std::to_string(need) + " B, got " +
+                std::to_string(ws_bytes));
+      return false;
+    }
+    return tc_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, radius, levels, cdtype, ymajor,
+                       scale, ws, ws_bytes, s);
+  }
+  if (!ok) return false;
+  return simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, radius, levels, dil, dtype,
+                       cdtype, ymajor, scale, s);
+}
+
+bool validate_layout(int B, int C, int H, int W, int dtype) {
+  if (dtype != LCB200_F32 && dtype != LCB200_F16) {
+    set_error("dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
+    return false;
+  }
+  if (C <= 0 || H < 0 || W < 0 || B < 0) {
+    set_error("invalid shape");
+    return false;
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace lcb200
+
+using namespace lcb200;
+
+extern "C" {
+
+bool launchLocalCorrCudaPyramidForward(const void* fmap1, const void* fmap2_packed,
+                                       const void* coords, void* corr, int B, int H1, int W1,
+                                       int C, int radius, int levels, int dilation, bool isHalf,
+                                       bool ymajor, cudaStream_t stream) {
+  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, C, radius, levels,
+                         dilation, isHalf ? LCB200_F16 : LCB200_F32,
+                         isHalf ? LCB200_F16 : LCB200_F32, ymajor, 1.0f, LCB200_ENGINE_AUTO,
+                         nullptr, 0, true, stream);
+}
+
+bool launchLocalCorrCudaPyramidBackward(const void* fmap1, const void* fmap2_packed,
+                                        const void* coords, const void* corr_grad,
+                                        void* fmap1_grad, float* fmap2_grad, int B, int H1,
+                                        int W1, int C, int radius, int levels, int dilation,
+                                        bool isHalf, bool ymajor, cudaStream_t stream) {
+  return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad, B, H1,
+                          W1, C, radius, levels, dilation, isHalf ? LCB200_F16 : LCB200_F32,
+                          isHalf ? LCB200_F16 : LCB200_F32, ymajor, 1.0f, true,
+                          LCB200_ENGINE_AUTO, nullptr, 0, true, stream);
+}
+
+size_t localCorrB200PyramidWorkspaceBytes(int B, int H1, int W1, int C, int radius, int levels,
+                                          int dilation, int dtype, int engine) {
+  bool empty = false;
+  clear_error();
+  if (!validate_pyramid(B, H1, W1, C, radius, levels, dilation, dtype, &empty) || empty)
+    return 0;
+  bool ok = true;
+  if (!use_tc(engine, B, H1, W1, C, radius, levels, dilation, dtype, &ok)) return 0;
+  return tc_workspace_bytes(B, H1, W1, C, radius, levels);
+}
+
+bool launchLocalCorrB200PyramidForward(const void* fmap1, const void* fmap2_packed,
+                                       const void* coords, void* corr, int B, int H1, int W1,
+                                       int C, int radius, int levels, int dilation, int dtype,
+                                       int coords_dtype, bool ymajor, float scale, int engine,
+                                       void* workspace, size_t workspace_bytes,
+                                       cudaStream_t stream) {
+  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, C, radius, levels,
+                         dilation, dtype, coords_dtype, ymajor, scale, engine, workspace,
+                         workspace_bytes, false, stream);
+}
+
+bool launchLocalCorrB200PyramidBackward(const void* fmap1, const void* fmap2_packed,
+                                        const void* coords, const void* corr_grad,
+                                        void* fmap1_grad, float* fmap2_grad_f32, int B, int H1,
+                                        int W1, int C, int radius, int levels, int dilation,
+                                        int dtype, int coords_dtype, bool ymajor, float scale,
+                                        bool accumulate, int engine, void* workspace,
+                                        size_t workspace_bytes, cudaStream_t stream) {
+  return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad_f32, B,
+                          H1, W1, C, radius, levels, dilation, dtype, coords_dtype, ymajor,
+                          scale, accumulate, engine, workspace, workspace_bytes, false, stream);
+}
+
+bool launchLocalCorrB200PyramidBuild(const void* fmap2_nchw, void* fmap2_packed, int B, int C,
+                                     int H, int W, int levels, int dtype, cudaStream_t stream) {
+  clear_error();
+  bool empty = false;
+  if (!validate_pyramid(B, H, W, C, 0, levels, 1, dtype, &empty)) return false;
+  if (empty) return true;
+  return layout_pyramid_build(fmap2_nchw, fmap2_packed, B, C, H, W, levels, dtype, stream);
+}
+
+bool launchLocalCorrB200PyramidBuildBackward(const void* grad_packed, bool grad_is_f32,
+                                             void* grad_fmap2_nchw, int B, int C, int H, int W,
+                                             int levels, int dtype, cudaStream_t stream) {
+  clear_error();
+  bool empty = false;
+  if (!validate_pyramid(B, H, W, C, 0, levels, 1, dtype, &empty)) return false;
+  if (empty) return true;
+  return layout_pyramid_build_grad(grad_packed, grad_is_f32, grad_fmap2_nchw, B, C, H, W,
+                                   levels, dtype, stream);
+}
+
+bool launchLocalCorrB200NchwToNhwc(const void* in, void* out, int B, int C, int HW, int dtype,
+                                   cudaStream_t stream) {
+  clear_error();
+  if (!validate_layout(B, C, HW, 1, dtype)) return false;
+  if (B == 0 || HW == 0) return true;
+  return layout_nchw_to_nhwc(in, out, B, C, HW, dtype, stream);
+}
+
+bool launchLocalCorrB200NhwcToNchw(const void* in, void* out, int B, int C, int HW, int dtype,
+                                   cudaStream_t stream) {
+  clear_error();
+  if (!validate_layout(B, C, HW, 1, dtype)) return false;
+  if (B == 0 || HW == 0) return true;
+  return layout_nhwc_to_nchw(in, out, B, C, HW, dtype, stream);
+}
+
+bool launchLocalCorrB200SpatialForward(const void* in1, const void* in2, void* out, int B, int C,
+                                       int H, int W, int radius, int dilation, int dtype,
+                                       float scale, cudaStream_t stream) {
+  clear_error();
+  if (!validate_layout(B, C, H, W, dtype)) return false;
+  if (radius < 0 || dilation < 1) {
+    set_error("spatial correlation needs radius >= 0 and dilation >= 1");
+    return false;
+  }
+  if (B == 0 || H == 0 || W == 0) return true;
+  return spatial_forward(in1, in2, out, B, C, H, W, radius, dilation, dtype, scale, stream);
+}
+
+bool launchLocalCorrB200SpatialBackward(const void* in1, const void* in2, const void* grad_out,
+                                        void* grad_in1, void* grad_in2, int B, int C, int H,
+                                        int W, int radius, int dilation, int dtype, float scale,
+                                        cudaStream_t stream) {
+  clear_error();
+  if (!validate_layout(B, C, H, W, dtype)) return false;
+  if (radius < 0 || dilation < 1) {
+    set_error("spatial correlation needs radius >= 0 and dilation >= 1");
+    return false;
+  }
+  if (B == 0 || H == 0 || W == 0) return true;
+  return spatial_backward(in1, in2, grad_out, grad_in1, grad_in2, B, C, H, W, radius, dilation,
+                          dtype, scale, stream);
+}
+
+const char* localCorrB200GetLastError(void) { return g_last_error.c_str(); }
+
+int localCorrB200Version(void) { return 100; }
+
+long long localCorrB200LaunchCount(int reset) {
+  const long long v = g_launches;
+  if (reset) g_launches = 0;
+  return v;
+}
+
+}  // extern "C"

@@ -1,0 +1,339 @@
+"""Tensor-level wrappers of the C ABI and their autograd Functions.
+
+Every op launches on torch's current CUDA stream of the input's device and
+allocates its outputs (and any engine workspace) from torch's caching
+allocator. Inputs must be CUDA tensors of dtype float32 or float16; there is
+no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float32: _lib.F32, torch.float16: _lib.F16}
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPES[t.dtype]
+    except KeyError:
+        raise RuntimeError(
+            f"localcorr_b200 requires float32 or float16 tensors, but got {t.dtype}."
+        ) from None
+
+
+def _require_cuda(*tensors: torch.Tensor, what: str = "localcorr_b200") -> None:
+    for t in tensors:
+        if not t.is_cuda:
+            raise RuntimeError(
+                f"{what} requires tensors on a CUDA device, but got a tensor on {t.device}."
+            )
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+# Optional launch timer: a list that receives (name, start_event, end_event)
+# for every engine call, recorded on the launching (current) stream. Used by
+# bench.py to time the dominant kernel live inside its timed region.
+_timer = None
+
+
+def set_launch_timer(records):
+    """Install (a list) or remove (None) the engine-call timer."""
+    global _timer
+    _timer = records
+
+
+def _timed(name, fn):
+    if _timer is None:
+        return fn()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    res = fn()
+    end.record()
+    _timer.append((name, start, end))
+    return res
+
+
+def level_shapes(h: int, w: int, levels: int) -> list[tuple[int, int]]:
+    """Floor-halved level dims of the pyramid (blocks.py:371-376)."""
+    return [(h >> l, w >> l) for l in range(levels)]
+
+
+def packed_row_elems(c: int, h: int, w: int, levels: int) -> int:
+    return sum(c * hl * wl for hl, wl in level_shapes(h, w, levels))
+
+
+# ---------------------------------------------------------------------------
+# raw launchers (no autograd)
+# ---------------------------------------------------------------------------
+
+def nchw_to_nhwc(x: torch.Tensor) -> torch.Tensor:
+    lib = _lib.require_library()
+    _require_cuda(x)
+    x = x.contiguous()
+    b, c, h, w = x.shape
+    out = torch.empty((b, h, w, c), dtype=x.dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        ok = lib.launchLocalCorrB200NchwToNhwc(x.data_ptr(), out.data_ptr(), b, c, h * w,
+                                               _dtype_code(x), _stream(x))
+    _lib.check(ok, "NCHW->NHWC transpose", lib)
+    return out
+
+
+def nhwc_to_nchw(x: torch.Tensor) -> torch.Tensor:
+    lib = _lib.require_library()
+    _require_cuda(x)
+    x = x.contiguous()
+    b, h, w, c = x.shape
+    out = torch.empty((b, c, h, w), dtype=x.dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        ok = lib.launchLocalCorrB200NhwcToNchw(x.data_ptr(), out.data_ptr(), b, c, h * w,
+                                               _dtype_code(x), _stream(x))
+    _lib.check(ok, "NHWC->NCHW transpose", lib)
+    return out
+
+
+def pyramid_build(fmap2: torch.Tensor, levels: int) -> torch.Tensor:
+    """fmap2 [B,C,H,W] -> batch-major packed NHWC pyramid [B, C*sum h_l*w_l]."""
+    lib = _lib.require_library()
+    _require_cuda(fmap2)
+    fmap2 = fmap2.contiguous()
+    b, c, h, w = fmap2.shape
+    packed = torch.empty((b, packed_row_elems(c, h, w, levels)), dtype=fmap2.dtype,
+                         device=fmap2.device)
+    with torch.cuda.device(fmap2.device):
+        ok = lib.launchLocalCorrB200PyramidBuild(fmap2.data_ptr(), packed.data_ptr(), b, c, h,
+                                                 w, levels, _dtype_code(fmap2), _stream(fmap2))
+    _lib.check(ok, "pyramid build", lib)
+    return packed
+
+
+def pyramid_build_backward(grad_packed: torch.Tensor, shape, levels: int,
+                           dtype: torch.dtype) -> torch.Tensor:
+    lib = _lib.require_library()
+    grad_packed = grad_packed.contiguous()
+    b, c, h, w = shape
+    out = torch.empty((b, c, h, w), dtype=dtype, device=grad_packed.device)
+    is_f32 = grad_packed.dtype == torch.float32
+    if not is_f32 and grad_packed.dtype != dtype:
+        grad_packed = grad_packed.to(dtype)
+    with torch.cuda.device(grad_packed.device):
+        ok = lib.launchLocalCorrB200PyramidBuildBackward(
+            grad_packed.data_ptr(), is_f32, out.data_ptr(), b, c, h, w, levels,
+            _DTYPES[dtype], _stream(grad_packed))
+    _lib.check(ok, "pyramid build backward", lib)
+    return out
+
+
+def workspace_bytes(b, h, w, c, radius, levels, dilation, dtype_code, engine) -> int:
+    lib = _lib.require_library()
+    return int(lib.localCorrB200PyramidWorkspaceBytes(b, h, w, c, radius, levels, dilation,
+                                                      dtype_code, engine))
+
+
+def _workspace(t: torch.Tensor, nbytes: int):
+    if nbytes == 0:
+        return None, 0
+    ws = torch.empty((nbytes + 255) // 256 * 256, dtype=torch.uint8, device=t.device)
+    return ws, ws.numel()
+
+
+def pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation=1,
+                         ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO) -> torch.Tensor:
+    """corr [B, L, RD^2, H, W] = scale * local correlation (extended C ABI)."""
+    lib = _lib.require_library()
+    b, h, w, c = fmap1.shape
+    rd = 2 * radius + 1
+    dt = _dtype_code(fmap1)
+    cdt = _dtype_code(coords)
+    corr = torch.empty((b, levels, rd * rd, h, w), dtype=fmap1.dtype, device=fmap1.device)
+    nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine)
+    ws, nws = _workspace(fmap1, nbytes)
+    with torch.cuda.device(fmap1.device):
+        ok = _timed("pyramid_fwd", lambda: lib.launchLocalCorrB200PyramidForward(
+            fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr.data_ptr(),
+            b, h, w, c, radius, levels, dilation, dt, cdt, bool(ymajor), float(scale), engine,
+            ws.data_ptr() if ws is not None else None, nws, _stream(fmap1)))
+    _lib.check(ok, "pyramid correlation forward", lib)
+    return corr
+
+
+def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels,
+                          dilation=1, ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO):
+    """Returns (grad_fmap1 [B,H,W,C] dtype, grad_fmap2_packed float32)."""
+    lib = _lib.require_library()
+    b, h, w, c = fmap1.shape
+    dt = _dtype_code(fmap1)
+    cdt = _dtype_code(coords)
+    corr_grad = corr_grad.contiguous()
+    if corr_grad.dtype != fmap1.dtype:
+        corr_grad = corr_grad.to(fmap1.dtype)
+    g1 = torch.empty_like(fmap1)
+    g2 = torch.empty(fmap2_packed.shape, dtype=torch.float32, device=fmap1.device)
+    nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine)
+    ws, nws = _workspace(fmap1, nbytes)
+    with torch.cuda.device(fmap1.device):
+        ok = _timed("pyramid_bwd", lambda: lib.launchLocalCorrB200PyramidBackward(
+            fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr_grad.data_ptr(),
+            g1.data_ptr(), g2.data_ptr(), b, h, w, c, radius, levels, dilation, dt, cdt,
+            bool(ymajor), float(scale), False, engine,
+            ws.data_ptr() if ws is not None else None, nws, _stream(fmap1)))
+    _lib.check(ok, "pyramid correlation backward", lib)
+    return g1, g2
+
+
+def spatial_forward(in1, in2, radius, dilation=1, scale=1.0) -> torch.Tensor:
+    lib = _lib.require_library()
+    b, c, h, w = in1.shape
+    rd = 2 * radius + 1
+    out = torch.empty((b, rd, rd, h, w), dtype=in1.dtype, device=in1.device)
+    with torch.cuda.device(in1.device):
+        ok = lib.launchLocalCorrB200SpatialForward(
+            in1.data_ptr(), in2.data_ptr(), out.data_ptr(), b, c, h, w, radius, dilation,
+            _dtype_code(in1), float(scale), _stream(in1))
+    _lib.check(ok, "spatial correlation forward", lib)
+    return out
+
+
+def spatial_backward(in1, in2, grad_out, radius, dilation=1, scale=1.0, need1=True,
+                     need2=True):
+    lib = _lib.require_library()
+    b, c, h, w = in1.shape
+    grad_out = grad_out.contiguous()
+    if grad_out.dtype != in1.dtype:
+        grad_out = grad_out.to(in1.dtype)
+    g1 = torch.empty_like(in1) if need1 else None
+    g2 = torch.empty_like(in2) if need2 else None
+    with torch.cuda.device(in1.device):
+        ok = lib.launchLocalCorrB200SpatialBackward(
+            in1.data_ptr(), in2.data_ptr(), grad_out.data_ptr(),
+            g1.data_ptr() if g1 is not None else None, g2.data_ptr() if g2 is not None else None,
+            b, c, h, w, radius, dilation, _dtype_code(in1), float(scale), _stream(in1))
+    _lib.check(ok, "spatial correlation backward", lib)
+    return g1, g2
+
+
+SPATIAL_KERNEL_MAX_RADIUS = 4
+
+
+# ---------------------------------------------------------------------------
+# autograd Functions
+# ---------------------------------------------------------------------------
+
+class NchwToNhwc(torch.autograd.Function):
+    """fmap1.permute(0, 2, 3, 1).contiguous() (blocks.py:370) as one kernel."""
+
+    @staticmethod
+    def forward(ctx, x):
+        return nchw_to_nhwc(x)
+
+    @staticmethod
+    def backward(ctx, g):
+        return nhwc_to_nchw(g)
+
+
+class PyramidBuild(torch.autograd.Function):
+    """avg_pool2d pyramid + NHWC + batch-major pack (blocks.py:371-383) in one kernel."""
+
+    @staticmethod
+    def forward(ctx, fmap2, levels):
+        ctx.shape = tuple(fmap2.shape)
+        ctx.levels = int(levels)
+        ctx.dtype = fmap2.dtype
+        return pyramid_build(fmap2, int(levels))
+
+    @staticmethod
+    def backward(ctx, g):
+        return pyramid_build_backward(g, ctx.shape, ctx.levels, ctx.dtype), None
+
+
+class ScaledPyramidCorr(torch.autograd.Function):
+    """scale * pyramid correlation, the fused form of the RAFT block call
+    (blocks.py:391-411: kernel launch, then reshape and division by sqrt(C))."""
+
+    @staticmethod
+    def forward(ctx, fmap1, fmap2_packed, coords, radius, levels, dilation, ymajor, scale):
+        coords = coords.contiguous()
+        corr = pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation,
+                                    ymajor, scale)
+        ctx.save_for_backward(fmap1, fmap2_packed, coords)
+        ctx.params = (int(radius), int(levels), int(dilation), bool(ymajor), float(scale))
+        return corr
+
+    @staticmethod
+    def backward(ctx, corr_grad):
+        fmap1, fmap2_packed, coords = ctx.saved_tensors
+        radius, levels, dilation, ymajor, scale = ctx.params
+        g1 = g2 = None
+        if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
+            g1, g2 = pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius,
+                                           levels, dilation, ymajor, scale)
+            if g2.dtype != fmap2_packed.dtype:
+                g2 = g2.to(fmap2_packed.dtype)
+        # RAFT detaches the sampling coordinates: zeros, as the reference
+        # returns (blocks.py:534-537).
+        gc = torch.zeros_like(coords) if ctx.needs_input_grad[2] else None
+        return g1, g2, gc, None, None, None, None, None
+
+
+class SpatialCorr(torch.autograd.Function):
+    """Spatial correlation on NCHW inputs, out [B, RD, RD, H, W]."""
+
+    @staticmethod
+    def forward(ctx, in1, in2, radius, dilation, scale):
+        in1 = in1.contiguous()
+        in2 = in2.contiguous()
+        out = spatial_forward(in1, in2, int(radius), int(dilation), float(scale))
+        ctx.save_for_backward(in1, in2)
+        ctx.params = (int(radius), int(dilation), float(scale))
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        in1, in2 = ctx.saved_tensors
+        radius, dilation, scale = ctx.params
+        g1, g2 = spatial_backward(in1, in2, g, radius, dilation, scale,
+                                  ctx.needs_input_grad[0], ctx.needs_input_grad[1])
+        return g1, g2, None, None, None
+
+
+def identity_coords(b, h, w, dtype, device) -> torch.Tensor:
+    """Identity grid [B, 2, H, W], channel 0 = x (blocks.py:615-620)."""
+    ys = torch.arange(h, device=device, dtype=dtype)
+    xs = torch.arange(w, device=device, dtype=dtype)
+    gy, gx = torch.meshgrid(ys, xs, indexing="ij")
+    return torch.stack([gx, gy], dim=0)[None].repeat(b, 1, 1, 1).contiguous()
+
+
+def spatial_corr(in1, in2, radius, dilation=1, scale=1.0) -> torch.Tensor:
+    """[B, RD, RD, H, W] spatial correlation of NCHW maps, any radius.
+
+    radius <= 4 runs the dedicated shift kernel; larger windows run the
+    pyramid engine with one level, y-major order and identity coordinates
+    (the route the reference's CUDA sampler always takes, blocks.py:682-694).
+    """
+    _require_cuda(in1, in2)
+    _dtype_code(in1)
+    if in2.dtype != in1.dtype:
+        raise RuntimeError("input1 and input2 must have the same dtype")
+    if radius <= SPATIAL_KERNEL_MAX_RADIUS:
+        return SpatialCorr.apply(in1, in2, radius, dilation, scale)
+    b, c, h, w = in1.shape
+    f1 = NchwToNhwc.apply(in1)
+    f2 = NchwToNhwc.apply(in2).reshape(b, -1)
+    coords = identity_coords(b, h, w, torch.float32, in1.device)
+    corr = ScaledPyramidCorr.apply(f1, f2, coords, radius, 1, dilation, True, scale)
+    rd = 2 * radius + 1
+    return corr.view(b, rd, rd, h, w)
+
+
+def default_scale(c: int) -> float:
+    return 1.0 / math.sqrt(c)

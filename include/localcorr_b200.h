@@ -155,6 +155,11 @@ LCB200_API bool launchLocalCorrB200SpatialBackward(
 /* Message of the last failed call on this thread ("" if none). */
 LCB200_API const char* localCorrB200GetLastError(void);
 
+/* Error status raised on the device by the tensor-core kernels (0 = none;
+ * 1 = a pipeline wait timed out and the kernel stopped early). Synchronises
+ * with the current device; reset clears it. */
+LCB200_API int localCorrB200DeviceStatus(int reset);
+
 /* Library ABI version (major*10000 + minor*100 + patch). */
 LCB200_API int localCorrB200Version(void);
 

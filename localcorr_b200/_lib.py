@@ -71,6 +71,7 @@ PROTOTYPES = {
         [_c_void_p] * 5 + [_c_int] * 7 + [_c_float, _c_void_p],
     ),
     "localCorrB200GetLastError": (ctypes.c_char_p, []),
+    "localCorrB200DeviceStatus": (_c_int, [_c_int]),
     "localCorrB200Version": (_c_int, []),
     "localCorrB200LaunchCount": (ctypes.c_longlong, [_c_int]),
 }

@@ -21,6 +21,9 @@ bool tc_forward(const void*, const void*, const void*, void*, int, int, int, int
                 int, bool, float, void*, size_t, cudaStream_t);
 bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int, int,
                  int, int, int, int, int, bool, float, void*, size_t, cudaStream_t);
+bool tc_bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
+                     int dtype, std::string* why);
+int tc_device_status(bool reset);
 bool layout_nchw_to_nhwc(const void*, void*, int, int, int, int, cudaStream_t);
 bool layout_nhwc_to_nchw(const void*, void*, int, int, int, int, cudaStream_t);
 bool layout_pyramid_build(const void*, void*, int, int, int, int, int, int, cudaStream_t);
@@ -160,11 +163,18 @@ void* library_scratch(size_t bytes, cudaStream_t s) {
 }
 
 bool use_tc(int engine, int B, int H1, int W1, int C, int radius, int levels, int dilation,
-            int dtype, bool* ok) {
+            int dtype, bool* ok, bool backward = false, const void* p1 = nullptr,
+            const void* p2 = nullptr) {
   *ok = true;
   if (engine == LCB200_ENGINE_SIMT) return false;
   std::string why;
-  const bool elig = tc_eligible(B, H1, W1, C, radius, levels, dilation, dtype, &why);
+  bool elig = backward ? tc_bwd_eligible(B, H1, W1, C, radius, levels, dilation, dtype, &why)
+                       : tc_eligible(B, H1, W1, C, radius, levels, dilation, dtype, &why);
+  // TMA and 16-byte cp.async need 16-byte aligned map bases.
+  if (elig && ((reinterpret_cast<uintptr_t>(p1) | reinterpret_cast<uintptr_t>(p2)) & 15)) {
+    elig = false;
+    why = "maps not 16-byte aligned";
+  }
   if (engine == LCB200_ENGINE_TC && !elig) {
     set_error("tensor-core engine not eligible: " + why);
     *ok = false;
@@ -191,7 +201,7 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
     return false;
   }
   bool ok = true;
-  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok)) {
+  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok, false, f1, f2)) {
     const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
     if (lib_ws) {
       ws = library_scratch(need, s);
@@ -229,7 +239,7 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
       return check_launch("memset fmap2_grad");
   }
   bool ok = true;
-  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok)) {
+  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok, true, f1, f2)) {
     const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
     if (lib_ws) {
       ws = library_scratch(need, s);
@@ -295,7 +305,10 @@ size_t localCorrB200PyramidWorkspaceBytes(int B, int H1, int W1, int C, int radi
   if (!validate_pyramid(B, H1, W1, C, radius, levels, dilation, dtype, &empty) || empty)
     return 0;
   bool ok = true;
-  if (!use_tc(engine, B, H1, W1, C, radius, levels, dilation, dtype, &ok)) return 0;
+  const bool f = use_tc(engine, B, H1, W1, C, radius, levels, dilation, dtype, &ok);
+  ok = true;
+  const bool b = use_tc(engine, B, H1, W1, C, radius, levels, dilation, dtype, &ok, true);
+  if (!f && !b) return 0;
   return tc_workspace_bytes(B, H1, W1, C, radius, levels);
 }
 
@@ -387,6 +400,8 @@ bool launchLocalCorrB200SpatialBackward(const void* in1, const void* in2, const 
 }
 
 const char* localCorrB200GetLastError(void) { return g_last_error.c_str(); }
+
+int localCorrB200DeviceStatus(int reset) { return tc_device_status(reset != 0); }
 
 int localCorrB200Version(void) { return 100; }
 

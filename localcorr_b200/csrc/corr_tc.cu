@@ -1,26 +1,701 @@
-// Tensor-core engine of the pyramid local correlation (placeholder until the
-// tcgen05 path lands: reports itself ineligible, so AUTO uses the SIMT engine).
+// Tensor-core (tcgen05 + TMA + TMEM) engine of the pyramid local correlation,
+// float16 maps, dilation 1, up to 4 levels, 64 <= C <= 256 (C % 64 == 0).
+//
+// Why a sort: every pixel needs the dot products of its fmap1 row with the
+// (2r+2)^2 fmap2 samples of its window, at every level. With arbitrary flow
+// the windows of neighbouring source pixels need not overlap, so a tile of
+// source pixels shares no fmap2 data and the work is a gather-GEMV. Bucketing
+// the pixels by where their windows land makes the sharing explicit:
+//
+//  1. sort    pixels are counting-sorted into anchor cells of 8x16 level-0
+//             base positions (floor of the level-0 coordinate). Cells are
+//             aligned to multiples of 8 (y) and 16 (x), so the level-l bases
+//             of a cell span (8>>l)x(16>>l) positions and the union of the
+//             cell's windows at level l is a fixed (8>>l)+2r+1 by
+//             (16>>l)+2r+1 box. Pixels whose windows miss the map at every
+//             level are dropped (their outputs are exact zeros).
+//  2. forward per chunk of <= 128 pixels of one cell: A = the chunk's fmap1
+//             rows (M=128, K=C), B = each level's union box of fmap2 loaded
+//             by TMA (N = union positions, K = C; out-of-map taps are the
+//             TMA zero fill, which is the reference's zero padding).
+//             tcgen05.mma accumulates S = A*B^T (fp32) in TMEM; TMEM lane m
+//             holds pixel m's row, so the epilogue thread of pixel m reads
+//             its window rows from TMEM and combines neighbouring grid
+//             samples with its bilinear weights:
+//               out(iy,ix) = wa*S[j][k] + wb*S[j][k+1] + wc*S[j+1][k] + wd*S[j+1][k+1]
+//             which equals the reference's tap-by-tap bilinear dot product
+//             (cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:139-272) by
+//             linearity. Outputs go to a scratch in sorted order.
+//  3. unsort  scratch rows are written to [B, L, RD^2, H, W] (coalesced
+//             along W), zeros for dropped pixels.
+//
+// Warp roles of the forward kernel (persistent, one CTA per SM):
+//   warp 0      producer: cp.async gather of the A tile, TMA loads of B boxes
+//   warp 1      TMEM owner and MMA issuer (one thread)
+//   warps 2..5  epilogue (TMEM lane quadrant = warp % 4)
+// Every mbarrier wait is bounded (2 s); on timeout the kernel records an
+// error status, all roles wind down, TMEM is freed and the kernel returns.
+#include <cub/block/block_scan.cuh>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <string>
+
 #include "lc_common.cuh"
+#include "tc_ptx.cuh"
 
 namespace lcb200 {
 
-bool tc_eligible(int, int, int, int, int, int, int, int, std::string* why) {
-  if (why) *why = "tensor-core engine not built";
-  return false;
+__device__ int g_tc_status = 0;
+
+namespace {
+
+constexpr int kCellY = 8, kCellX = 16, kTile = 128;
+constexpr int kMaxTcLevels = 4;
+constexpr int kFwdThreads = 192;
+
+struct TcGeom {
+  int B, H, W, C, r, L, RD, RD2, RDP, KC, HW;
+  int ylo, xlo, yhi, xhi, ncy, ncx, ncell;
+  int h[kMaxTcLevels], w[kMaxTcLevels];
+  long long off[kMaxTcLevels];
+  long long batch_elems;
+  int UH[kMaxTcLevels], UW[kMaxTcLevels], R[kMaxTcLevels], nparts[kMaxTcLevels],
+      npad[kMaxTcLevels];
+  int maxN, nld, RS;
+  long long npix;  // B*HW
+};
+
+inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+inline int round_up(int a, int b) { return ceil_div(a, b) * b; }
+
+bool make_tc_geom(int B, int H, int W, int C, int r, int L, TcGeom* g, std::string* why) {
+  TcGeom t{};
+  t.B = B; t.H = H; t.W = W; t.C = C; t.r = r; t.L = L;
+  t.RD = 2 * r + 1;
+  t.RD2 = t.RD * t.RD;
+  t.RDP = round_up(t.RD2, 8);
+  t.KC = C / 64;
+  t.HW = H * W;
+  t.npix = (long long)B * H * W;
+  const int s = 1 << (L - 1);
+  // Bases outside [lo, hi) have windows outside the map at every level.
+  t.ylo = -round_up((r + 2) * s, kCellY);
+  t.xlo = -round_up((r + 2) * s, kCellX);
+  t.yhi = H + (r + 1) * s;
+  t.xhi = W + (r + 1) * s;
+  t.ncy = ceil_div(t.yhi - t.ylo, kCellY);
+  t.ncx = ceil_div(t.xhi - t.xlo, kCellX);
+  t.ncell = t.ncy * t.ncx;
+  long long acc = 0;
+  for (int l = 0; l < L; ++l) {
+    t.h[l] = H >> l;
+    t.w[l] = W >> l;
+    t.off[l] = acc;
+    acc += (long long)C * t.h[l] * t.w[l];
+  }
+  t.batch_elems = acc;
+  t.UW[0] = kCellX + 2 * r + 1;
+  t.nld = ceil_div(t.UW[0], 32);
+  t.RS = 32 * t.nld + 4;
+  t.maxN = 0;
+  for (int l = 0; l < L; ++l) {
+    t.UH[l] = (kCellY >> l) + 2 * r + 1;
+    t.UW[l] = (kCellX >> l) + 2 * r + 1;
+    // Rows per part: the part must fit one 256-column TMEM buffer, including
+    // the 32*nld-column window read of its last row.
+    const int rmax = std::min(256 / t.UW[l], (256 - 32 * t.nld) / t.UW[l] + 1);
+    if (rmax < 2) {
+      if (why) *why = "union rows too wide for a TMEM buffer";
+      return false;
+    }
+    int np = std::max(1, ceil_div(t.UH[l] - 1, rmax - 1));
+    int R = ceil_div(t.UH[l] - 1, np) + 1;
+    if (R > t.UH[l]) R = t.UH[l];
+    t.nparts[l] = np;
+    t.R[l] = R;
+    t.npad[l] = round_up(R * t.UW[l], 16);
+    t.maxN = std::max(t.maxN, t.npad[l]);
+  }
+  *g = t;
+  return true;
 }
 
-size_t tc_workspace_bytes(int, int, int, int, int, int) { return 0; }
+struct alignas(64) TcFwdParams {
+  CUtensorMap tmap[kMaxTcLevels];
+  const __half* fmap1;
+  const void* coords;
+  const int* sorted;
+  const int4* work;
+  const int* work_count;
+  __half* scratch;
+  float scale;
+  int coords_f32;
+  int ymajor;
+  int nstage;
+  uint32_t stage_bytes;
+  TcGeom g;
+};
 
-bool tc_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
-                int, bool, float, void*, size_t, cudaStream_t) {
-  set_error("tensor-core engine not built");
+// ---------------------------------------------------------------------------
+// sort: histogram -> scan (+ work list) -> scatter
+// ---------------------------------------------------------------------------
+template <typename TC>
+__global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ counts,
+                               int2* __restrict__ keyrank, TcGeom g) {
+  const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (gid >= g.npix) return;
+  const int b = (int)(gid / g.HW);
+  const int p = (int)(gid - (long long)b * g.HW);
+  const float cx = ldf(coords + (long long)b * 2 * g.HW + p);
+  const float cy = ldf(coords + (long long)b * 2 * g.HW + g.HW + p);
+  const float fx = floorf(cx), fy = floorf(cy);
+  int2 kr = make_int2(-1, 0);
+  if (fx >= (float)g.xlo && fx < (float)g.xhi && fy >= (float)g.ylo && fy < (float)g.yhi) {
+    const int bx = (int)fx, by = (int)fy;
+    const int cell = ((by - g.ylo) / kCellY) * g.ncx + (bx - g.xlo) / kCellX;
+    kr.x = cell;
+    kr.y = atomicAdd(counts + (long long)b * g.ncell + cell, 1);
+  }
+  keyrank[gid] = kr;
+}
+
+// One CTA: exclusive scan of the per-cell counts (cell offsets into the
+// sorted order) and of the per-cell chunk counts (work-list offsets), then
+// the work list itself: {b, cell, first sorted index, pixel count <= 128}.
+__global__ void __launch_bounds__(1024)
+tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
+               int4* __restrict__ work, int* __restrict__ work_count, int ncell_total,
+               int ncell) {
+  using Scan = cub::BlockScan<int2, 1024>;
+  __shared__ typename Scan::TempStorage tmp;
+  __shared__ int carry[2];
+  if (threadIdx.x == 0) { carry[0] = 0; carry[1] = 0; }
+  __syncthreads();
+  for (int base = 0; base < ncell_total; base += 1024) {
+    const int i = base + threadIdx.x;
+    const int cnt = i < ncell_total ? counts[i] : 0;
+    const int nch = (cnt + kTile - 1) / kTile;
+    int2 in = make_int2(cnt, nch), ex, tot;
+    // Scan both values with a pair-sum operator.
+    struct Pair { __device__ int2 operator()(int2 a, int2 b) const { return make_int2(a.x + b.x, a.y + b.y); } };
+    Scan(tmp).ExclusiveScan(in, ex, make_int2(0, 0), Pair(), tot);
+    const int off = carry[0] + ex.x;
+    const int coff = carry[1] + ex.y;
+    if (i < ncell_total) {
+      offsets[i] = off;
+      const int b = i / ncell;
+      const int cell = i - b * ncell;
+      for (int j = 0; j < nch; ++j)
+        work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { carry[0] += tot.x; carry[1] += tot.y; }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *work_count = carry[1];
+}
+
+__global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* __restrict__ offsets,
+                                  int* __restrict__ sorted, int* __restrict__ inv, TcGeom g) {
+  const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (gid >= g.npix) return;
+  const int2 kr = keyrank[gid];
+  if (kr.x < 0) {
+    inv[gid] = -1;
+    return;
+  }
+  const int b = (int)(gid / g.HW);
+  const int pos = offsets[(long long)b * g.ncell + kr.x] + kr.y;
+  sorted[pos] = (int)gid;
+  inv[gid] = pos;
+}
+
+// ---------------------------------------------------------------------------
+// forward
+// ---------------------------------------------------------------------------
+template <int RADIUS>
+__global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
+  constexpr int RD = 2 * RADIUS + 1;
+  constexpr int NW = RD + 1;  // grid samples per window row
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int abort_flag;
+  const TcGeom& g = p.g;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = sA + g.KC * 16384;
+  const int NST = p.nstage;
+  const int RDPS = g.RDP / 2 + 1;  // smem output row stride in 32-bit words (odd)
+  uint32_t* sOut = reinterpret_cast<uint32_t*>(sB + (size_t)NST * p.stage_bytes);
+  float* sRow = reinterpret_cast<float*>(sOut + kTile * RDPS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + kTile * g.RS);
+  uint64_t* full = bars;
+  uint64_t* empty = bars + NST;
+  uint64_t* a_full = bars + 2 * NST;
+  uint64_t* a_empty = a_full + 1;
+  uint64_t* t_full = a_full + 2;   // [2]
+  uint64_t* t_empty = a_full + 4;  // [2]
+  uint64_t* epi_bar = a_full + 6;  // epilogue-wide sync (bounded, unlike bar.sync)
+  uint64_t* fin_bar = a_full + 7;  // all MMAs of this CTA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_full + 8);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
+    tc::mbar_init(a_full, 1);
+    tc::mbar_init(a_empty, 1);
+    for (int i = 0; i < 2; ++i) { tc::mbar_init(t_full + i, 1); tc::mbar_init(t_empty + i, kTile); }
+    tc::mbar_init(epi_bar, kTile);
+    tc::mbar_init(fin_bar, 1);
+    tc::fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nwork = *p.work_count;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    uint32_t gs = 0;
+    int it = 0;
+    for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x, ++it) {
+      const int4 wk = p.work[wi];
+      const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
+      if (!tc::mbar_wait(a_empty, (it & 1) ^ 1, abort)) break;
+      // A tile: 128 rows x C fp16, K-major SWIZZLE_128B, 64-channel slabs.
+      const int units = g.KC * 8;
+      for (int idx = lane; idx < kTile * units; idx += 32) {
+        const int t = idx / units;
+        const int u = idx - t * units;
+        const int kc = u >> 3, j = u & 7;
+        uint8_t* dst = sA + kc * 16384 + t * 128 + ((j ^ (t & 7)) << 4);
+        if (t < n) {
+          const int gid = p.sorted[start + t];
+          tc::cp_async_16(dst, p.fmap1 + (long long)gid * g.C + kc * 64 + j * 8, 16);
+        } else {
+          tc::cp_async_16(dst, p.fmap1, 0);
+        }
+      }
+      tc::cp_async_wait_all();
+      tc::fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) tc::mbar_arrive(a_full);
+      const int cy = cell / g.ncx, cx = cell - cy * g.ncx;
+      const int cell_y0 = g.ylo + cy * kCellY, cell_x0 = g.xlo + cx * kCellX;
+      bool ok = true;
+      for (int l = 0; l < g.L && ok; ++l) {
+        const int X0 = (cell_x0 >> l) - RADIUS;
+        const int Y0 = (cell_y0 >> l) - RADIUS;
+        const uint32_t box = 128u * g.UW[l] * g.R[l];
+        for (int k = 0; k < g.nparts[l] && ok; ++k) {
+          for (int kc = 0; kc < g.KC; ++kc, ++gs) {
+            const int s = gs % NST;
+            const uint32_t use = gs / NST;
+            if (lane == 0) {
+              if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; }
+              else {
+                tc::mbar_arrive_expect_tx(full + s, box);
+                tc::tma_load_4d(sB + (size_t)s * p.stage_bytes, &p.tmap[l], full + s, kc * 64,
+                                X0, Y0 + k * (g.R[l] - 1), b);
+              }
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+          }
+        }
+      }
+      if (!ok) break;
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t gs = 0, pc = 0;
+      int it = 0;
+      const uint32_t a_base = tc::smem_u32(sA);
+      const uint32_t b_base = tc::smem_u32(sB);
+      bool ok = true;
+      for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
+        if (!tc::mbar_wait(a_full, it & 1, abort)) break;
+        tc::tc_fence_after();
+        for (int l = 0; l < g.L && ok; ++l) {
+          const uint32_t idesc = tc::idesc_f16_f32(128, g.npad[l], false, false);
+          for (int k = 0; k < g.nparts[l] && ok; ++k, ++pc) {
+            const int buf = pc & 1;
+            if (!tc::mbar_wait(t_empty + buf, ((pc >> 1) & 1) ^ 1, abort)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint32_t d = tmem + buf * 256;
+            for (int kc = 0; kc < g.KC; ++kc, ++gs) {
+              const int s = gs % NST;
+              const uint32_t use = gs / NST;
+              if (!tc::mbar_wait(full + s, use & 1, abort)) { ok = false; break; }
+              tc::tc_fence_after();
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk) {
+                const uint64_t ad = tc::smem_desc_sw128(a_base + kc * 16384 + kk * 32, 16, 1024);
+                const uint64_t bd = tc::smem_desc_sw128(b_base + s * p.stage_bytes + kk * 32, 16, 1024);
+                tc::mma_f16_ss(d, ad, bd, idesc, (kc | kk) != 0);
+              }
+              tc::mma_commit(empty + s);
+            }
+            if (!ok) break;
+            tc::mma_commit(t_full + buf);
+          }
+        }
+        if (ok) tc::mma_commit(a_empty);
+      }
+      // Drain: TMEM is freed only after every issued MMA has completed.
+      tc::mma_commit(fin_bar);
+      tc::mbar_wait(fin_bar, 0, abort);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;           // TMEM lane quadrant of this warp
+    const int t = q * 32 + lane;      // tile row = pixel slot
+    const int et = threadIdx.x - 64;  // 0..127 for the cooperative copy
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    float* myrow = sRow + t * g.RS;
+    uint32_t pc = 0, ephase = 0;
+    bool ok = true;
+    auto epi_sync = [&]() -> bool {
+      tc::mbar_arrive(epi_bar);
+      return tc::mbar_wait(epi_bar, (ephase++) & 1, abort);
+    };
+    for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x) {
+      const int4 wk = p.work[wi];
+      const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
+      const bool valid = t < n;
+      float cx = 0.f, cy = 0.f;
+      if (valid) {
+        const int gid = p.sorted[start + t];
+        const int pix = gid - b * g.HW;
+        if (p.coords_f32) {
+          const float* co = reinterpret_cast<const float*>(p.coords) + (long long)b * 2 * g.HW + pix;
+          cx = co[0]; cy = co[g.HW];
+        } else {
+          const __half* co = reinterpret_cast<const __half*>(p.coords) + (long long)b * 2 * g.HW + pix;
+          cx = __half2float(co[0]); cy = __half2float(co[g.HW]);
+        }
+      }
+      const int ccy = cell / g.ncx, ccx = cell - ccy * g.ncx;
+      const int cell_y0 = g.ylo + ccy * kCellY, cell_x0 = g.xlo + ccx * kCellX;
+      for (int l = 0; l < g.L && ok; ++l) {
+        const float inv = 1.f / (float)(1 << l);
+        const float clx = cx * inv, cly = cy * inv;
+        const float x0f = floorf(clx), y0f = floorf(cly);
+        const float dx = clx - x0f, dy = cly - y0f;
+        const float wa = (1.f - dx) * (1.f - dy), wb = dx * (1.f - dy);
+        const float wc = (1.f - dx) * dy, wd = dx * dy;
+        const int rx = (int)x0f - (cell_x0 >> l);
+        const int ry = (int)y0f - (cell_y0 >> l);
+        const int UW = g.UW[l], UH = g.UH[l], R = g.R[l];
+        float prev[NW], cur[NW];
+#pragma unroll
+        for (int k = 0; k < NW; ++k) prev[k] = 0.f;
+        for (int k = 0; k < g.nparts[l]; ++k, ++pc) {
+          const int buf = pc & 1;
+          if (!tc::mbar_wait(t_full + buf, (pc >> 1) & 1, abort)) { ok = false; break; }
+          tc::tc_fence_after();
+          const int U0 = k * (R - 1);
+          for (int u = 0; u < R; ++u) {
+            const int U = U0 + u;
+            if (U >= UH) break;
+            for (int c = 0; c < g.nld; ++c) {
+              float v[32];
+              tc::tmem_ld32(lane_addr + buf * 256 + u * UW + 32 * c, v);
+              tc::tmem_ld_wait();
+#pragma unroll
+              for (int i = 0; i < 32; i += 4)
+                *reinterpret_cast<float4*>(myrow + 32 * c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+            }
+            const int j = U - ry;  // window row of this grid row
+            if (valid && j >= 0 && j <= RD) {
+#pragma unroll
+              for (int k2 = 0; k2 < NW; ++k2) cur[k2] = myrow[rx + k2];
+              if (u > 0 && j >= 1) {
+                const int iy = j - 1;
+#pragma unroll
+                for (int ix = 0; ix < RD; ++ix) {
+                  const float val = wa * prev[ix] + wb * prev[ix + 1] + wc * cur[ix] + wd * cur[ix + 1];
+                  const int d = p.ymajor ? (ix + RD * iy) : (iy + RD * ix);
+                  reinterpret_cast<__half*>(sOut + t * RDPS)[d] = __float2half_rn(val * p.scale);
+                }
+              }
+#pragma unroll
+              for (int k2 = 0; k2 < NW; ++k2) prev[k2] = cur[k2];
+            }
+          }
+          tc::tc_fence_before();
+          tc::mbar_arrive(t_empty + buf);
+        }
+        if (!ok) break;
+        // Level complete for this chunk: copy the staged rows to the scratch.
+        if (!epi_sync()) { ok = false; break; }
+        const int words = g.RDP / 2;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(p.scratch + ((long long)l * g.npix + start) * g.RDP);
+        for (int i = et; i < n * words; i += kTile) {
+          const int row = i / words;
+          const int wd2 = i - row * words;
+          dst[i] = sOut[row * RDPS + wd2];
+        }
+        if (!epi_sync()) { ok = false; break; }
+      }
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && abort_flag) atomicExch(&g_tc_status, 1);
+}
+
+// scratch [L][npix][RDP] (sorted order) -> out [B][L][RD2][H][W]
+__global__ void tc_unsort_kernel(const __half* __restrict__ scratch, const int* __restrict__ inv,
+                                 __half* __restrict__ out, TcGeom g) {
+  const int pix = blockIdx.x * blockDim.x + threadIdx.x;
+  const int l = blockIdx.y;
+  const int b = blockIdx.z;
+  if (pix >= g.HW) return;
+  const long long gid = (long long)b * g.HW + pix;
+  const int idx = inv[gid];
+  const __half* src = scratch + ((long long)l * g.npix + (idx < 0 ? 0 : idx)) * g.RDP;
+  __half* dst = out + ((long long)b * g.L + l) * g.RD2 * g.HW + pix;
+  for (int d0 = 0; d0 < g.RD2; d0 += 8) {
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (idx >= 0) v = *reinterpret_cast<const uint4*>(src + d0);
+    const __half* hv = reinterpret_cast<const __half*>(&v);
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      if (d0 + e < g.RD2) dst[(long long)(d0 + e) * g.HW] = hv[e];
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host
+// ---------------------------------------------------------------------------
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+int num_sms() {
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  return v > 0 ? v : 1;
+}
+
+struct WsLayout {
+  size_t counts, offsets, keyrank, sorted, inv, work, work_count, scratch, total;
+  long long max_work;
+};
+
+size_t align256(size_t v) { return (v + 255) & ~size_t(255); }
+
+WsLayout ws_layout(const TcGeom& g) {
+  WsLayout w{};
+  size_t o = 0;
+  const size_t ncells = (size_t)g.B * g.ncell;
+  w.max_work = (g.npix + kTile - 1) / kTile + (long long)ncells;
+  w.counts = o; o = align256(o + ncells * 4);
+  w.offsets = o; o = align256(o + ncells * 4);
+  w.keyrank = o; o = align256(o + (size_t)g.npix * 8);
+  w.sorted = o; o = align256(o + (size_t)g.npix * 4);
+  w.inv = o; o = align256(o + (size_t)g.npix * 4);
+  w.work = o; o = align256(o + (size_t)w.max_work * 16);
+  w.work_count = o; o = align256(o + 4);
+  w.scratch = o; o = align256(o + (size_t)g.L * g.npix * g.RDP * 2);
+  w.total = o;
+  return w;
+}
+
+size_t fwd_smem_bytes(const TcGeom& g, int nstage, uint32_t* stage_bytes) {
+  const uint32_t sb = (uint32_t)g.maxN * 128;
+  if (stage_bytes) *stage_bytes = sb;
+  const size_t rdps = g.RDP / 2 + 1;
+  const size_t need = 1024 /*alignment slack*/ + (size_t)g.KC * 16384 + (size_t)nstage * sb +
+                      (size_t)kTile * rdps * 4 + (size_t)kTile * g.RS * 4 + (2 * nstage + 8) * 8 +
+                      16;
+  // At least half of the SM's shared memory: one CTA per SM, so the
+  // 512-column TMEM allocation never waits on a co-resident CTA.
+  return std::max<size_t>(need, 120 * 1024);
+}
+
+bool radius_supported(int r) { return r == 3 || r == 4 || r == 8; }
+
+bool eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation, int dtype,
+              std::string* why, TcGeom* out_geom, int* out_nstage) {
+  auto no = [&](const char* m) { if (why) *why = m; return false; };
+  if (dtype != LCB200_F16) return no("tensor-core engine needs float16 maps");
+  if (dilation != 1) return no("tensor-core engine needs dilation 1");
+  if (levels < 1 || levels > kMaxTcLevels) return no("tensor-core engine supports 1..4 levels");
+  if (C % 64 != 0 || C < 64 || C > 256) return no("tensor-core engine needs C in {64,128,192,256}");
+  if (!radius_supported(radius)) return no("tensor-core engine radius not instantiated");
+  TcGeom g;
+  if (!make_tc_geom(B, H1, W1, C, radius, levels, &g, why)) return false;
+  if ((long long)B * H1 * W1 >= (1ll << 31)) return no("too many pixels");
+  const size_t lim = (size_t)max_dyn_smem();
+  int nst = 4;
+  while (nst >= 2 && fwd_smem_bytes(g, nst, nullptr) > lim) --nst;
+  if (nst < 2) return no("tensor-core engine shared-memory budget exceeded");
+  if (out_geom) *out_geom = g;
+  if (out_nstage) *out_nstage = nst;
+  return true;
+}
+
+template <int RADIUS>
+bool launch_fwd_kernel(const TcFwdParams& prm, size_t smem, cudaStream_t s) {
+  auto k = tc_fwd_kernel<RADIUS>;
+  if (!ensure_smem_attr((const void*)k, smem)) return false;
+  k<<<num_sms(), kFwdThreads, smem, s>>>(prm);
+  count_launch();
+  return check_launch("tc_fwd");
+}
+
+}  // namespace
+
+bool tc_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation, int dtype,
+                 std::string* why) {
+  return eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, nullptr, nullptr);
+}
+
+size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels) {
+  TcGeom g;
+  if (!make_tc_geom(B, H1, W1, C, radius, levels, &g, nullptr)) return 0;
+  return ws_layout(g).total;
+}
+
+bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1, int W1,
+                int C, int radius, int levels, int cdtype, bool ymajor, float scale, void* ws,
+                size_t ws_bytes, cudaStream_t s) {
+  TcGeom g;
+  int nst = 0;
+  std::string why;
+  if (!eligible(B, H1, W1, C, radius, levels, 1, LCB200_F16, &why, &g, &nst)) {
+    set_error("tensor-core forward: " + why);
+    return false;
+  }
+  const WsLayout L = ws_layout(g);
+  if (ws_bytes < L.total) {
+    set_error("tensor-core forward: workspace too small");
+    return false;
+  }
+  auto encode = get_encode_fn();
+  if (!encode) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return false;
+  }
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  int* counts = reinterpret_cast<int*>(w + L.counts);
+  int* offsets = reinterpret_cast<int*>(w + L.offsets);
+  int2* keyrank = reinterpret_cast<int2*>(w + L.keyrank);
+  int* sorted = reinterpret_cast<int*>(w + L.sorted);
+  int* inv = reinterpret_cast<int*>(w + L.inv);
+  int4* work = reinterpret_cast<int4*>(w + L.work);
+  int* work_count = reinterpret_cast<int*>(w + L.work_count);
+  __half* scratch = reinterpret_cast<__half*>(w + L.scratch);
+
+  if (cudaMemsetAsync(counts, 0, sizeof(int) * (size_t)B * g.ncell, s) != cudaSuccess)
+    return check_launch("memset counts");
+  const int threads = 256;
+  const int blocks = (int)((g.npix + threads - 1) / threads);
+  if (cdtype == LCB200_F32)
+    tc_hist_kernel<float><<<blocks, threads, 0, s>>>((const float*)co, counts, keyrank, g);
+  else
+    tc_hist_kernel<__half><<<blocks, threads, 0, s>>>((const __half*)co, counts, keyrank, g);
+  count_launch();
+  if (!check_launch("tc_hist")) return false;
+  tc_scan_kernel<<<1, 1024, 0, s>>>(counts, offsets, work, work_count, B * g.ncell, g.ncell);
+  count_launch();
+  if (!check_launch("tc_scan")) return false;
+  tc_scatter_kernel<<<blocks, threads, 0, s>>>(keyrank, offsets, sorted, inv, g);
+  count_launch();
+  if (!check_launch("tc_scatter")) return false;
+
+  TcFwdParams prm;
+  memset(&prm, 0, sizeof(prm));
+  for (int l = 0; l < levels; ++l) {
+    const __half* base = static_cast<const __half*>(f2) + g.off[l];
+    cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)g.w[l], (cuuint64_t)g.h[l], (cuuint64_t)B};
+    cuuint64_t strides[3] = {(cuuint64_t)C * 2, (cuuint64_t)g.w[l] * C * 2,
+                             (cuuint64_t)g.batch_elems * 2};
+    cuuint32_t box[4] = {64, (cuuint32_t)g.UW[l], (cuuint32_t)g.R[l], 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = encode(&prm.tmap[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, (void*)base, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled failed for level " + std::to_string(l) + " (CUresult " +
+                std::to_string((int)r) + ")");
+      return false;
+    }
+  }
+  prm.fmap1 = static_cast<const __half*>(f1);
+  prm.coords = co;
+  prm.sorted = sorted;
+  prm.work = work;
+  prm.work_count = work_count;
+  prm.scratch = scratch;
+  prm.scale = scale;
+  prm.coords_f32 = cdtype == LCB200_F32;
+  prm.ymajor = ymajor ? 1 : 0;
+  prm.nstage = nst;
+  prm.g = g;
+  const size_t smem = fwd_smem_bytes(g, nst, &prm.stage_bytes);
+  bool ok = false;
+  switch (radius) {
+    case 3: ok = launch_fwd_kernel<3>(prm, smem, s); break;
+    case 4: ok = launch_fwd_kernel<4>(prm, smem, s); break;
+    case 8: ok = launch_fwd_kernel<8>(prm, smem, s); break;
+    default: set_error("radius not instantiated"); return false;
+  }
+  if (!ok) return false;
+  dim3 ug((g.HW + 127) / 128, levels, B);
+  tc_unsort_kernel<<<ug, 128, 0, s>>>(scratch, inv, static_cast<__half*>(out), g);
+  count_launch();
+  return check_launch("tc_unsort");
+}
+
+bool tc_bwd_eligible(int, int, int, int, int, int, int, int, std::string* why) {
+  if (why) *why = "tensor-core backward not built";
   return false;
 }
 
 bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int, int,
                  int, int, int, int, int, bool, float, void*, size_t, cudaStream_t) {
-  set_error("tensor-core engine not built");
+  set_error("tensor-core backward not built");
   return false;
+}
+
+int tc_device_status(bool reset) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_tc_status, sizeof(int));
+  if (reset) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_tc_status, &z, sizeof(int));
+  }
+  return v;
 }
 
 }  // namespace lcb200

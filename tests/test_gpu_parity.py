@@ -111,7 +111,7 @@ PYR_CASES = [
     (1, 3, 9, 11, 2, 1, 2.0),     # tiny C
     (1, 32, 20, 24, 2, 0, 2.0),   # radius 0
     (1, 128, 16, 32, 4, 8, 20.0), # radius 8 (configuration 5)
-    (2, 16, 64, 8, 5, 2, 4.0),    # 5 levels (beyond the fused pyramid build)
+    (2, 16, 64, 40, 5, 2, 4.0),   # 5 levels (beyond the fused pyramid build)
 ]
 
 
@@ -281,7 +281,7 @@ def test_far_outside_coords_exact_zeros_and_no_grad():
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=["f32", "f16"])
 @pytest.mark.parametrize("shape,levels", [((2, 40, 37, 70), 4), ((1, 8, 135, 240), 4),
-                                          ((1, 5, 300, 9), 6)])
+                                          ((1, 5, 300, 70), 6)])
 def test_pyramid_build_matches_torch_chain(shape, levels, dtype):
     x = torch.randn(shape, generator=torch.Generator().manual_seed(1)).to(DEV, dtype)
     packed = ops.pyramid_build(x, levels)

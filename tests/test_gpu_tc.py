@@ -1,0 +1,147 @@
+"""Tensor-core engine (tcgen05/TMA) parity: forward against the float64 oracle
+and against the SIMT engine, across flow fields that stress the pixel sort
+(i.i.d. Gaussian flow with far out-of-bounds pixels, smooth flow, uniform
++-64 flow, converging flow that overfills one anchor cell), radii, channel
+counts, level counts, channel orders and coords dtypes. Float16 tolerance:
+rtol 1e-2 / atol 1e-2 against the oracle on the same float16 inputs."""
+
+import math
+
+import pytest
+import torch
+
+from localcorr_b200 import _lib, ops
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+F16TOL = dict(rtol=1e-2, atol=1e-2)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_gpu():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    assert _lib.load_library() is not None
+
+
+@pytest.fixture(autouse=True)
+def _device_status_clean():
+    lib = _lib.load_library()
+    lib.localCorrB200DeviceStatus(1)
+    yield
+    assert lib.localCorrB200DeviceStatus(1) == 0, "a tensor-core pipeline wait timed out"
+
+
+def _coords(kind, b, h, w, seed):
+    if kind == "gauss_oob":
+        return oracle.make_coords_gauss_oob(b, h, w, 6.0, 0.05, seed=seed)
+    if kind == "smooth":
+        return oracle.make_coords_smooth(b, h, w, 40.0, seed=seed)
+    if kind == "uniform64":
+        return oracle.make_coords_uniform(b, h, w, 64.0, seed=seed)
+    if kind == "converge":
+        # Every pixel looks at (almost) the same spot: one anchor cell gets
+        # all of them (many 128-pixel chunks), the rest stay empty.
+        g = torch.Generator().manual_seed(seed)
+        c = torch.empty(b, 2, h, w)
+        c[:, 0] = w / 2 + torch.rand(b, h, w, generator=g) * 3
+        c[:, 1] = h / 2 + torch.rand(b, h, w, generator=g) * 3
+        return c
+    return oracle.make_coords_uniform(b, h, w, 8.0, seed=seed)
+
+
+def _inputs(b, c, h, w, levels, kind, seed=0):
+    f1, f2 = oracle.make_fmaps(b, c, h, w, seed=seed)
+    f1, f2 = f1.half(), f2.half()
+    co = _coords(kind, b, h, w, seed + 1)
+    fm1 = ops.nchw_to_nhwc(f1.to(DEV))
+    packed = ops.pyramid_build(f2.to(DEV), levels)
+    return f1, f2, co, fm1, packed
+
+
+CASES = [
+    # b, c, h, w, levels, radius, coords
+    (2, 256, 40, 52, 4, 4, "gauss_oob"),
+    (1, 256, 47, 61, 4, 4, "smooth"),
+    (2, 128, 32, 64, 4, 4, "uniform64"),
+    (1, 128, 33, 70, 4, 3, "gauss_oob"),
+    (1, 128, 30, 40, 4, 8, "uniform64"),
+    (1, 64, 24, 36, 2, 4, "uniform8"),
+    (1, 192, 20, 28, 1, 4, "uniform8"),
+    (1, 256, 24, 40, 3, 3, "converge"),
+]
+
+
+@pytest.mark.parametrize("case", CASES, ids=lambda c: "b{}c{}_{}x{}_l{}r{}_{}".format(*c))
+def test_tc_forward_vs_oracle(case):
+    b, c, h, w, levels, r, kind = case
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, kind)
+    co16 = co.half()
+    ref = oracle.pyramid_corr(f1.float(), f2.float(), co16.float(), levels, r)
+    scale = 1.0 / math.sqrt(c)
+    out = ops.pyramid_corr_forward(fm1, packed, co16.to(DEV), r, levels, 1, False, scale,
+                                   _lib.ENGINE_TC)
+    torch.testing.assert_close(out.double().cpu(), ref * scale, **F16TOL)
+    simt = ops.pyramid_corr_forward(fm1, packed, co16.to(DEV), r, levels, 1, False, scale,
+                                    _lib.ENGINE_SIMT)
+    torch.testing.assert_close(out.float(), simt.float(), rtol=2e-3, atol=2e-3)
+
+
+def test_tc_forward_ymajor_and_fp32_coords():
+    b, c, h, w, levels, r = 1, 128, 36, 44, 3, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "gauss_oob", seed=3)
+    ref = oracle.pyramid_corr(f1.float(), f2.float(), co, levels, r, ymajor=True)
+    out = ops.pyramid_corr_forward(fm1, packed, co.to(DEV), r, levels, 1, True, 1.0,
+                                   _lib.ENGINE_TC)
+    torch.testing.assert_close(out.double().cpu() / math.sqrt(c), ref / math.sqrt(c), **F16TOL)
+
+
+def test_tc_forward_all_out_of_bounds_is_zero():
+    b, c, h, w, levels, r = 1, 64, 16, 32, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "uniform8")
+    co = torch.full((b, 2, h, w), 5000.0, dtype=torch.float16)
+    out = ops.pyramid_corr_forward(fm1, packed, co.to(DEV), r, levels, 1, False, 1.0,
+                                   _lib.ENGINE_TC)
+    assert torch.count_nonzero(out) == 0
+
+
+def test_tc_forward_repeatable():
+    b, c, h, w, levels, r = 2, 256, 40, 52, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "gauss_oob", seed=5)
+    a = ops.pyramid_corr_forward(fm1, packed, co.half().to(DEV), r, levels, 1, False, 1.0,
+                                 _lib.ENGINE_TC)
+    bb = ops.pyramid_corr_forward(fm1, packed, co.half().to(DEV), r, levels, 1, False, 1.0,
+                                  _lib.ENGINE_TC)
+    assert torch.equal(a, bb)
+
+
+def test_tc_reference_abi_uses_library_scratch():
+    # The reference-compatible launcher takes no workspace: the library's
+    # own stream-ordered scratch serves the tensor-core engine.
+    import localcorr_b200 as lc
+
+    b, c, h, w, levels, r = 1, 256, 30, 50, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "gauss_oob", seed=6)
+    out = lc.LocalCorrCudaPyramidFunction.apply(fm1, packed, co.half().to(DEV), r, levels, 1,
+                                                False)
+    ref = oracle.pyramid_corr(f1.float(), f2.float(), co.half().float(), levels, r)
+    torch.testing.assert_close(out.double().cpu() / 16, ref / 16, **F16TOL)
+
+
+def test_tc_config2_shape_spot_check():
+    b, c, h, w, levels, r = 2, 256, 135, 240, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "gauss_oob", seed=8)
+    co16 = co.half()
+    out = ops.pyramid_corr_forward(fm1, packed, co16.to(DEV), r, levels, 1, False,
+                                   1.0 / 16, _lib.ENGINE_TC)
+    g = torch.Generator().manual_seed(3)
+    n = 400
+    pts = torch.stack([torch.randint(0, b, (n,), generator=g), torch.randint(0, h, (n,), generator=g),
+                       torch.randint(0, w, (n,), generator=g)], 1)
+    ref = oracle.pyramid_corr_points(f1.float(), f2.float(), co16.float(), levels, r, pts)
+    got = out.float().cpu()[pts[:, 0], :, :, pts[:, 1], pts[:, 2]]
+    torch.testing.assert_close(got.double(), ref / 16, **F16TOL)
+    simt = ops.pyramid_corr_forward(fm1, packed, co16.to(DEV), r, levels, 1, False, 1.0 / 16,
+                                    _lib.ENGINE_SIMT)
+    torch.testing.assert_close(out.float(), simt.float(), rtol=2e-3, atol=2e-3)

@@ -64,6 +64,13 @@ struct TcGeom {
       npad[kMaxTcLevels];
   int maxN, nld, RS;
   long long npix;  // B*HW
+  // backward: integer-grid weights per pixel/level ((RD+1)^2, padded), the
+  // union row groups of <= 64 positions (grad_fmap1 K chunks), and the
+  // output-tile work decomposition of grad_fmap2
+  int NG, RDQ;
+  int Rg[kMaxTcLevels], ngroups[kMaxTcLevels];
+  int nqy[kMaxTcLevels], nqx[kMaxTcLevels], rpi[kMaxTcLevels], qgroups[kMaxTcLevels];
+  long long items_before[kMaxTcLevels + 1];  // grad_fmap2 items, coarse levels first
 };
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
@@ -116,6 +123,33 @@ bool make_tc_geom(int B, int H, int W, int C, int r, int L, TcGeom* g, std::stri
     t.R[l] = R;
     t.npad[l] = round_up(R * t.UW[l], 16);
     t.maxN = std::max(t.maxN, t.npad[l]);
+  }
+  t.NG = t.RD + 1;
+  t.RDQ = round_up(t.NG * t.NG, 8);
+  for (int l = 0; l < L; ++l) {
+    if (t.UW[l] > 64) {
+      if (why) *why = "union rows wider than 64 positions";
+      return false;
+    }
+    t.Rg[l] = 64 / t.UW[l];
+    t.ngroups[l] = ceil_div(t.UH[l], t.Rg[l]);
+    // grad_fmap2 tiles of 8x16 level-l positions; a tile pulls the pixels of
+    // the anchor cells whose level-l windows can reach it, split into items
+    // of rpi cell rows.
+    t.nqy[l] = ceil_div(t.h[l], 8);
+    t.nqx[l] = ceil_div(t.w[l], 16);
+    const int span_y = (8 + 2 * r + 1) << l;   // level-0 rows of bases that can touch a tile
+    const int span_x = (16 + 2 * r + 1) << l;
+    const int rows = span_y / kCellY + 2;
+    const int cols = span_x / kCellX + 2;
+    t.rpi[l] = std::max(1, 16 / cols);
+    t.qgroups[l] = ceil_div(rows, t.rpi[l]);
+  }
+  t.items_before[0] = 0;
+  for (int i = 0; i < L; ++i) {
+    const int l = L - 1 - i;  // coarse levels first (longest items first)
+    t.items_before[i + 1] =
+        t.items_before[i] + (long long)B * t.nqy[l] * t.nqx[l] * t.qgroups[l];
   }
   *g = t;
   return true;
@@ -460,6 +494,619 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_con
   if (threadIdx.x == 0 && abort_flag) atomicExch(&g_tc_status, 1);
 }
 
+// ---------------------------------------------------------------------------
+// backward
+// ---------------------------------------------------------------------------
+// The gradient of one tap spreads over its four grid corners, so per pixel
+// and level the incoming gradient collapses onto the (RD+1)^2 integer grid:
+//   G[j][k] = scale * ( g(j,k)*wa + g(j,k-1)*wb + g(j-1,k)*wc + g(j-1,k-1)*wd )
+// (terms with an index outside [0, RD) omitted). Then
+//   grad_fmap1[p]  = sum_l sum_{j,k} G_l[p][j][k] * fmap2_l[y0-r+j][x0-r+k]
+//   grad_fmap2_l[q] = sum_p G_l[p][q - (y0-r, x0-r)] * fmap1[p]
+// which are the reference backward's per-tap sums
+// (cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:887-916) regrouped.
+
+// Source-order pass: reads corr_grad (coalesced along W), writes the pixel's
+// G rows in sorted order gint[l][idx][RDQ] (fp16), and zeroes grad_fmap1 of
+// pixels dropped by the sort (windows off the map at every level).
+template <int RADIUS>
+__global__ void __launch_bounds__(128)
+tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
+               int coords_f32, const int* __restrict__ inv, __half* __restrict__ gint,
+               __half* __restrict__ grad_f1, float scale, int ymajor, TcGeom g) {
+  constexpr int RD = 2 * RADIUS + 1;
+  constexpr int NG = RD + 1;
+  const int pix = blockIdx.x * blockDim.x + threadIdx.x;
+  const int l = blockIdx.y;
+  const int b = blockIdx.z;
+  if (pix >= g.HW) return;
+  const long long gid = (long long)b * g.HW + pix;
+  const int idx = inv[gid];
+  if (idx < 0) {
+    if (l == 0) {
+      uint4* row = reinterpret_cast<uint4*>(grad_f1 + gid * g.C);
+      for (int i = 0; i < g.C / 8; ++i) row[i] = make_uint4(0, 0, 0, 0);
+    }
+    return;
+  }
+  float cx, cy;
+  if (coords_f32) {
+    const float* co = reinterpret_cast<const float*>(coords) + (long long)b * 2 * g.HW + pix;
+    cx = co[0]; cy = co[g.HW];
+  } else {
+    const __half* co = reinterpret_cast<const __half*>(coords) + (long long)b * 2 * g.HW + pix;
+    cx = __half2float(co[0]); cy = __half2float(co[g.HW]);
+  }
+  const float inv_s = 1.f / (float)(1 << l);
+  const float clx = cx * inv_s, cly = cy * inv_s;
+  const float dx = clx - floorf(clx), dy = cly - floorf(cly);
+  const float wa = (1.f - dx) * (1.f - dy) * scale, wb = dx * (1.f - dy) * scale;
+  const float wc = (1.f - dx) * dy * scale, wd = dx * dy * scale;
+  const __half* src = corr_grad + ((long long)b * g.L + l) * RD * RD * g.HW + pix;
+  float gr[RD * RD];
+#pragma unroll
+  for (int d = 0; d < RD * RD; ++d) gr[d] = __half2float(src[(long long)d * g.HW]);
+  auto gv = [&](int iy, int ix) -> float {
+    return gr[ymajor ? (ix + RD * iy) : (iy + RD * ix)];
+  };
+  uint4* dst = reinterpret_cast<uint4*>(gint + ((long long)l * g.npix + idx) * g.RDQ);
+#pragma unroll
+  for (int e0 = 0; e0 < NG * NG; e0 += 8) {
+    __align__(16) __half hv[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int ee = e0 + e;
+      float v = 0.f;
+      if (ee < NG * NG) {
+        const int j = ee / NG, k = ee % NG;
+        if (j < RD && k < RD) v += gv(j, k) * wa;
+        if (j < RD && k >= 1) v += gv(j, k - 1) * wb;
+        if (j >= 1 && k < RD) v += gv(j - 1, k) * wc;
+        if (j >= 1 && k >= 1) v += gv(j - 1, k - 1) * wd;
+      }
+      hv[e] = __float2half_rn(v);
+    }
+    dst[e0 / 8] = *reinterpret_cast<const uint4*>(hv);
+  }
+}
+
+struct alignas(64) TcBwdParams {
+  CUtensorMap tmap[kMaxTcLevels];
+  const void* coords;
+  const int* sorted;
+  const int* counts;
+  const int* offsets;
+  const int4* work;
+  const int* work_count;
+  const __half* gint;
+  const __half* fmap1;
+  __half* grad_f1;
+  float* grad_f2;
+  int coords_f32;
+  int nstage;
+  uint32_t stage_bytes;
+  long long nitems;
+  TcGeom g;
+};
+
+__device__ __forceinline__ void pixel_coords(const TcBwdParams& p, int b, int pix, float& cx,
+                                             float& cy) {
+  const TcGeom& g = p.g;
+  if (p.coords_f32) {
+    const float* co = reinterpret_cast<const float*>(p.coords) + (long long)b * 2 * g.HW + pix;
+    cx = co[0]; cy = co[g.HW];
+  } else {
+    const __half* co = reinterpret_cast<const __half*>(p.coords) + (long long)b * 2 * g.HW + pix;
+    cx = __half2float(co[0]); cy = __half2float(co[g.HW]);
+  }
+}
+
+// grad_fmap1, per 128-pixel chunk: D[128 px x C] += G[128 px x 64 pos] *
+// F2[64 pos x C] over every union row group of every level; D lives in TMEM
+// for the whole chunk, so each pixel row is written once (no atomics).
+// A (G rows) is built by the builder warps (K-major, SWIZZLE_128B); B is the
+// union row group loaded by TMA and read as an MN-major operand (channels
+// contiguous), the same boxes the forward reads K-major.
+template <int RADIUS>
+__global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_constant__ TcBwdParams p) {
+  constexpr int RD = 2 * RADIUS + 1;
+  constexpr int NG = RD + 1;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int abort_flag;
+  const TcGeom& g = p.g;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NST = p.nstage;
+  const uint32_t SB = p.stage_bytes;  // 16 KB of A + KC * 8 KB of B
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * SB);
+  uint64_t* bfull = bars;
+  uint64_t* afull = bars + NST;
+  uint64_t* empty = bars + 2 * NST;
+  uint64_t* acc_full = bars + 3 * NST;
+  uint64_t* acc_empty = acc_full + 1;
+  uint64_t* fin_bar = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 3);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  // Zero every stage once: the rows of a B stage past the current box (and
+  // never loaded yet) must hold finite values for the padded K positions.
+  for (int i = threadIdx.x; i < (int)(NST * SB / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  tc::fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      tc::mbar_init(bfull + s, 1);
+      tc::mbar_init(afull + s, kTile);
+      tc::mbar_init(empty + s, 1);
+    }
+    tc::mbar_init(acc_full, 1);
+    tc::mbar_init(acc_empty, kTile);
+    tc::mbar_init(fin_bar, 1);
+    tc::fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == 1) {
+    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int nwork = *p.work_count;
+  volatile int* abort = &abort_flag;
+
+  if (warp == 0) {
+    // ---------------- producer: B = union row groups ----------------
+    if (lane == 0) {
+      uint32_t gs = 0;
+      bool ok = true;
+      for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x) {
+        const int4 wk = p.work[wi];
+        const int b = wk.x, cell = wk.y;
+        const int cy = cell / g.ncx, cx = cell - cy * g.ncx;
+        const int cell_y0 = g.ylo + cy * kCellY, cell_x0 = g.xlo + cx * kCellX;
+        for (int l = 0; l < g.L && ok; ++l) {
+          const int X0 = (cell_x0 >> l) - RADIUS;
+          const int Y0 = (cell_y0 >> l) - RADIUS;
+          const uint32_t box = 128u * g.UW[l] * g.Rg[l];
+          for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
+            const int s = gs % NST;
+            const uint32_t use = gs / NST;
+            if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
+            tc::mbar_arrive_expect_tx(bfull + s, box * g.KC);
+            uint8_t* sb = smem + (size_t)s * SB + 16384;
+            for (int kc = 0; kc < g.KC; ++kc)
+              tc::tma_load_4d(sb + kc * 8192, &p.tmap[l], bfull + s, kc * 64, X0,
+                              Y0 + gi * g.Rg[l], b);
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t gs = 0;
+      int it = 0;
+      const uint32_t base = tc::smem_u32(smem);
+      const uint32_t idesc = tc::idesc_f16_f32(128, g.C, false, true);
+      bool ok = true;
+      for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
+        if (!tc::mbar_wait(acc_empty, (it & 1) ^ 1, abort)) break;
+        tc::tc_fence_after();
+        bool first = true;
+        for (int l = 0; l < g.L && ok; ++l) {
+          for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
+            const int s = gs % NST;
+            const uint32_t use = gs / NST;
+            if (!tc::mbar_wait(bfull + s, use & 1, abort) ||
+                !tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
+            tc::tc_fence_after();
+            const uint32_t sa = base + s * SB;
+            const uint32_t sb = sa + 16384;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t ad = tc::smem_desc_sw128(sa + kk * 32, 16, 1024);
+              const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, 8192, 1024);
+              tc::mma_f16_ss(tmem, ad, bd, idesc, first ? 0u : 1u);
+              first = false;
+            }
+            tc::mma_commit(empty + s);
+          }
+        }
+        if (ok) tc::mma_commit(acc_full);
+      }
+      tc::mma_commit(fin_bar);
+      tc::mbar_wait(fin_bar, 0, abort);
+    }
+    __syncwarp();
+  } else {
+    // ---------------- builders + epilogue ----------------
+    const int q = warp & 3;
+    const int t = q * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t gs = 0;
+    int it = 0;
+    bool ok = true;
+    for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
+      const int4 wk = p.work[wi];
+      const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
+      const bool valid = t < n;
+      const int idx = start + t;
+      int gid = 0;
+      float cx = 0.f, cy = 0.f;
+      if (valid) {
+        gid = p.sorted[idx];
+        pixel_coords(p, b, gid - b * g.HW, cx, cy);
+      }
+      const int ccy = cell / g.ncx, ccx = cell - ccy * g.ncx;
+      const int cell_y0 = g.ylo + ccy * kCellY, cell_x0 = g.xlo + ccx * kCellX;
+      for (int l = 0; l < g.L && ok; ++l) {
+        const float inv = 1.f / (float)(1 << l);
+        const int rx = (int)floorf(cx * inv) - (cell_x0 >> l);
+        const int ry = (int)floorf(cy * inv) - (cell_y0 >> l);
+        const int UW = g.UW[l], Rg = g.Rg[l];
+        const __half* grow = p.gint + ((long long)l * g.npix + idx) * g.RDQ;
+        for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
+          const int s = gs % NST;
+          const uint32_t use = gs / NST;
+          if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
+          uint8_t* arow = smem + (size_t)s * SB + t * 128;
+#pragma unroll
+          for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(arow)[j] = make_uint4(0, 0, 0, 0);
+          if (valid) {
+            const int u0 = max(gi * Rg, ry), u1 = min(gi * Rg + Rg - 1, ry + RD);
+            for (int U = u0; U <= u1; ++U) {
+              const int jrow = U - ry;
+              const int pos0 = (U - gi * Rg) * UW + rx;
+#pragma unroll
+              for (int k = 0; k < NG; ++k) {
+                const int pos = pos0 + k;
+                *reinterpret_cast<__half*>(arow + (((pos >> 3) ^ (t & 7)) << 4) + (pos & 7) * 2) =
+                    grow[jrow * NG + k];
+              }
+            }
+          }
+          tc::fence_proxy_async_smem();
+          tc::mbar_arrive(afull + s);
+        }
+      }
+      if (!ok) break;
+      // epilogue: TMEM row t = this pixel's grad_fmap1 (fp32) -> fp16 row
+      if (!tc::mbar_wait(acc_full, it & 1, abort)) { ok = false; break; }
+      tc::tc_fence_after();
+      for (int c0 = 0; c0 < g.C; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(lane_addr + c0, v);
+        tc::tmem_ld_wait();
+        if (valid) {
+          uint4* dst = reinterpret_cast<uint4*>(p.grad_f1 + (long long)gid * g.C + c0);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            __align__(16) __half2 h2[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) h2[e] = __floats2half2_rn(v[8 * i + 2 * e], v[8 * i + 2 * e + 1]);
+            dst[i] = *reinterpret_cast<const uint4*>(h2);
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(acc_empty);
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 256);
+  }
+  if (threadIdx.x == 0 && abort_flag) atomicExch(&g_tc_status, 1);
+}
+
+// grad_fmap2, pulled per output tile Q of 8x16 level-l positions:
+//   D[128 pos x C] = sum over the pixels whose windows reach Q of
+//                    G^T[pos x px] * fmap1[px x C]
+// The candidate pixels are the contiguous sorted ranges of the anchor cells
+// that can reach Q; builders keep those whose window intersects Q, writing
+// per kept pixel one row of A (MN-major: 128 position weights) and one row of
+// B (MN-major: the fmap1 row, cp.async). D is double-buffered in TMEM; the
+// epilogue adds it to the float32 gradient with red.global.add.v4.f32 (an
+// item may cover only part of Q's cells, so items of one Q add up).
+constexpr int kBwd2Threads = 288;  // warp 0 MMA, 1-4 builders, 5-8 epilogue
+
+struct Bwd2Item {
+  int l, b, qy0, qx0, ra, rb, ca, cb;  // level, batch, tile origin, cell rows/cols
+  bool empty;
+};
+
+__device__ __forceinline__ Bwd2Item decode_item(const TcGeom& g, long long it, int radius) {
+  Bwd2Item r{};
+  int li = 0;
+  while (li + 1 < g.L && it >= g.items_before[li + 1]) ++li;
+  const int l = g.L - 1 - li;
+  long long rem = it - g.items_before[li];
+  const int grp = (int)(rem % g.qgroups[l]);
+  rem /= g.qgroups[l];
+  const int qtx = (int)(rem % g.nqx[l]);
+  rem /= g.nqx[l];
+  const int qty = (int)(rem % g.nqy[l]);
+  const int b = (int)(rem / g.nqy[l]);
+  r.l = l;
+  r.b = b;
+  r.qy0 = qty * 8;
+  r.qx0 = qtx * 16;
+  const int s = 1 << l;
+  // level-l bases that can touch Q, then the level-0 base range, then cells
+  const int by_lo = (r.qy0 - radius - 1) * s, by_hi = (r.qy0 + 7 + radius) * s + s - 1;
+  const int bx_lo = (r.qx0 - radius - 1) * s, bx_hi = (r.qx0 + 15 + radius) * s + s - 1;
+  int ra = (by_lo - g.ylo) >= 0 ? (by_lo - g.ylo) / kCellY : 0;
+  int rb = (by_hi - g.ylo) >= 0 ? (by_hi - g.ylo) / kCellY : -1;
+  int ca = (bx_lo - g.xlo) >= 0 ? (bx_lo - g.xlo) / kCellX : 0;
+  int cb = (bx_hi - g.xlo) >= 0 ? (bx_hi - g.xlo) / kCellX : -1;
+  rb = min(rb, g.ncy - 1);
+  cb = min(cb, g.ncx - 1);
+  ra = ra + grp * g.rpi[l];
+  rb = min(rb, ra + g.rpi[l] - 1);
+  r.ra = ra; r.rb = rb; r.ca = ca; r.cb = cb;
+  r.empty = ra > rb || ca > cb;
+  return r;
+}
+
+template <int RADIUS>
+__global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_constant__ TcBwdParams p) {
+  constexpr int RD = 2 * RADIUS + 1;
+  constexpr int NG = RD + 1;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ int abort_flag;
+  __shared__ int wcount[4];
+  __shared__ int stage_flags[8];   // bit0: last stage of the item, bit1: item has pixels
+  const TcGeom& g = p.g;
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int NST = p.nstage;
+  const uint32_t SB = p.stage_bytes;  // A: 2 x 16 KB, B: KC x 16 KB
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * SB);
+  uint64_t* afull = bars;
+  uint64_t* empty = bars + NST;
+  uint64_t* acc_full = bars + 2 * NST;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* bsync_bar = acc_full + 4;    // builder-wide bounded sync
+  uint64_t* fin_bar = acc_full + 5;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 6);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  for (int i = threadIdx.x; i < (int)(NST * SB / 16); i += blockDim.x)
+    reinterpret_cast<uint4*>(smem)[i] = make_uint4(0, 0, 0, 0);
+  tc::fence_proxy_async_smem();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < NST; ++s) {
+      tc::mbar_init(afull + s, kTile);
+      tc::mbar_init(empty + s, 1);
+    }
+    for (int i = 0; i < 2; ++i) { tc::mbar_init(acc_full + i, 1); tc::mbar_init(acc_empty + i, kTile); }
+    tc::mbar_init(bsync_bar, kTile);
+    tc::mbar_init(fin_bar, 1);
+    tc::fence_mbar_init();
+    abort_flag = 0;
+  }
+  if (warp == 0) {
+    tc::tmem_alloc(tmem_slot, 512);
+    tc::tmem_relinquish();
+  }
+  tc::tc_fence_before();
+  __syncthreads();
+  tc::tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  volatile int* abort = &abort_flag;
+  const long long nitems = p.nitems;
+
+  if (warp == 0) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      uint32_t gs = 0, ac = 0;
+      const uint32_t base = tc::smem_u32(smem);
+      const uint32_t idesc = tc::idesc_f16_f32(128, g.C, true, true);
+      bool ok = true;
+      for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++ac) {
+        const int buf = ac & 1;
+        if (!tc::mbar_wait(acc_empty + buf, ((ac >> 1) & 1) ^ 1, abort)) break;
+        tc::tc_fence_after();
+        bool first = true;
+        for (;;) {
+          const int s = gs % NST;
+          const uint32_t use = gs / NST;
+          if (!tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
+          tc::tc_fence_after();
+          const int flags = stage_flags[s];
+          const uint32_t sa = base + s * SB;
+          const uint32_t sb = sa + 32768;
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t ad = tc::smem_desc_sw128(sa + kk * 2048, 16384, 1024);
+            const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, 16384, 1024);
+            tc::mma_f16_ss(tmem + buf * 256, ad, bd, idesc, first ? 0u : 1u);
+            first = false;
+          }
+          tc::mma_commit(empty + s);
+          ++gs;
+          if (flags & 1) break;
+        }
+        if (!ok) break;
+        tc::mma_commit(acc_full + buf);
+      }
+      tc::mma_commit(fin_bar);
+      tc::mbar_wait(fin_bar, 0, abort);
+    }
+    __syncwarp();
+  } else if (warp <= 4) {
+    // ---------------- builders ----------------
+    const int bw = warp - 1;          // builder warp 0..3
+    const int bt = bw * 32 + lane;    // builder thread 0..127
+    uint32_t gs = 0, bphase = 0;
+    bool ok = true;
+    auto bsync = [&]() -> bool {
+      tc::mbar_arrive(bsync_bar);
+      return tc::mbar_wait(bsync_bar, (bphase++) & 1, abort);
+    };
+    const unsigned lt_mask = (1u << lane) - 1u;
+    for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      const Bwd2Item item = decode_item(g, it, RADIUS);
+      const int l = item.l, b = item.b;
+      const int hl = g.h[l], wl = g.w[l];
+      const float inv = 1.f / (float)(1 << l);
+      int fill = 0;        // rows used in the current stage (uniform)
+      bool any = false;    // item has at least one pixel (uniform)
+      int s = gs % NST;
+      if (!tc::mbar_wait(empty + s, ((gs / NST) & 1) ^ 1, abort)) { ok = false; break; }
+      for (int cyr = item.ra; cyr <= item.rb && ok && !item.empty; ++cyr) {
+        const long long c0 = (long long)b * g.ncell + (long long)cyr * g.ncx + item.ca;
+        const long long c1 = (long long)b * g.ncell + (long long)cyr * g.ncx + item.cb;
+        const int s0 = p.offsets[c0];
+        const int s1 = p.offsets[c1] + p.counts[c1];
+        for (int base = s0; base < s1 && ok; base += kTile) {
+          const int pos = base + bt;
+          bool touch = false;
+          int gid = 0, x0 = 0, y0 = 0;
+          if (pos < s1) {
+            gid = p.sorted[pos];
+            float cx, cy;
+            pixel_coords(p, b, gid - b * g.HW, cx, cy);
+            x0 = (int)floorf(cx * inv);
+            y0 = (int)floorf(cy * inv);
+            // window rows y0-r..y0+r+1 meet Q rows qy0..qy0+7 (and the map)
+            const int ylo = max(max(y0 - RADIUS, item.qy0), 0);
+            const int yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
+            const int xlo = max(max(x0 - RADIUS, item.qx0), 0);
+            const int xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
+            touch = ylo <= yhi && xlo <= xhi;
+          }
+          const unsigned ballot = __ballot_sync(0xffffffffu, touch);
+          if (lane == 0) wcount[bw] = __popc(ballot);
+          if (!bsync()) { ok = false; break; }
+          int woff = 0, total = 0;
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const int c = wcount[w];
+            woff += (w < bw) ? c : 0;
+            total += c;
+          }
+          if (!bsync()) { ok = false; break; }
+          if (total == 0) continue;
+          any = true;
+          const int slot = fill + woff + __popc(ballot & lt_mask);
+          // Rows that fit the current stage, then the overflow into the next.
+          auto write_row = [&](int st, int row) {
+            uint8_t* A = smem + (size_t)st * SB;
+            uint8_t* Bm = A + 32768;
+            // A row: this pixel's G restricted to Q (position = 16*dy + dx)
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                *reinterpret_cast<uint4*>(A + m * 16384 + row * 128 + (j << 4)) = make_uint4(0, 0, 0, 0);
+            const __half* grow = p.gint + ((long long)l * g.npix + pos) * g.RDQ;
+            const int ylo = max(max(y0 - RADIUS, item.qy0), 0);
+            const int yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
+            const int xlo = max(max(x0 - RADIUS, item.qx0), 0);
+            const int xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
+            for (int yy = ylo; yy <= yhi; ++yy) {
+              for (int xx = xlo; xx <= xhi; ++xx) {
+                const int pq = (yy - item.qy0) * 16 + (xx - item.qx0);
+                const int m = pq >> 6, cc = pq & 63;
+                *reinterpret_cast<__half*>(A + m * 16384 + row * 128 + ((((cc >> 3) ^ (row & 7))) << 4) +
+                                           (cc & 7) * 2) =
+                    grow[(yy - (y0 - RADIUS)) * NG + (xx - (x0 - RADIUS))];
+              }
+            }
+            // B row: the pixel's fmap1 row, 64-channel blocks
+            const __half* f1 = p.fmap1 + (long long)gid * g.C;
+            for (int kc = 0; kc < g.KC; ++kc)
+#pragma unroll
+              for (int j = 0; j < 8; ++j)
+                tc::cp_async_16(Bm + kc * 16384 + row * 128 + ((j ^ (row & 7)) << 4),
+                                f1 + kc * 64 + j * 8, 16);
+          };
+          if (touch && slot < kTile) write_row(s, slot);
+          if (fill + total >= kTile) {
+            // current stage complete: publish it
+            tc::cp_async_wait_all();
+            tc::fence_proxy_async_smem();
+            if (bt == 0) stage_flags[s] = 2;  // not last, item has pixels
+            tc::mbar_arrive(afull + s);
+            ++gs;
+            s = gs % NST;
+            if (!tc::mbar_wait(empty + s, ((gs / NST) & 1) ^ 1, abort)) { ok = false; break; }
+            if (touch && slot >= kTile) write_row(s, slot - kTile);
+            fill = fill + total - kTile;
+          } else {
+            fill += total;
+          }
+        }
+      }
+      if (!ok) break;
+      // Close the item: zero the unused rows of the current stage (A only;
+      // stale B rows are finite and meet zero weights), flag it last.
+      if (bt >= fill) {
+        uint8_t* A = smem + (size_t)s * SB;
+#pragma unroll
+        for (int m = 0; m < 2; ++m)
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            *reinterpret_cast<uint4*>(A + m * 16384 + bt * 128 + (j << 4)) = make_uint4(0, 0, 0, 0);
+      }
+      tc::cp_async_wait_all();
+      tc::fence_proxy_async_smem();
+      if (bt == 0) stage_flags[s] = 1 | (any ? 2 : 0);
+      tc::mbar_arrive(afull + s);
+      ++gs;
+    }
+  } else {
+    // ---------------- epilogue ----------------
+    const int q = warp & 3;
+    const int t = q * 32 + lane;   // D row = position in Q
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    uint32_t ac = 0, gs_seen = 0;
+    (void)gs_seen;
+    for (long long it = blockIdx.x; it < nitems; it += gridDim.x, ++ac) {
+      const int buf = ac & 1;
+      if (!tc::mbar_wait(acc_full + buf, (ac >> 1) & 1, abort)) break;
+      tc::tc_fence_after();
+      const Bwd2Item item = decode_item(g, it, RADIUS);
+      const int l = item.l;
+      const int qy = item.qy0 + (t >> 4), qx = item.qx0 + (t & 15);
+      const bool inmap = !item.empty && qy < g.h[l] && qx < g.w[l];
+      float* dst = p.grad_f2 + (long long)item.b * g.batch_elems + g.off[l] +
+                   ((long long)qy * g.w[l] + qx) * g.C;
+      for (int c0 = 0; c0 < g.C; c0 += 32) {
+        float v[32];
+        tc::tmem_ld32(lane_addr + buf * 256 + c0, v);
+        tc::tmem_ld_wait();
+        if (inmap) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) {
+            if (v[i] != 0.f || v[i + 1] != 0.f || v[i + 2] != 0.f || v[i + 3] != 0.f)
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst + c0 + i),
+                           "f"(v[i]), "f"(v[i + 1]), "f"(v[i + 2]), "f"(v[i + 3])
+                           : "memory");
+          }
+        }
+      }
+      tc::tc_fence_before();
+      tc::mbar_arrive(acc_empty + buf);
+    }
+  }
+
+  tc::tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc::tc_fence_after();
+    tc::tmem_dealloc(tmem, 512);
+  }
+  if (threadIdx.x == 0 && abort_flag) atomicExch(&g_tc_status, 1);
+}
+
 // scratch [L][npix][RDP] (sorted order) -> out [B][L][RD2][H][W]
 __global__ void tc_unsort_kernel(const __half* __restrict__ scratch, const int* __restrict__ inv,
                                  __half* __restrict__ out, TcGeom g) {
@@ -524,9 +1171,55 @@ WsLayout ws_layout(const TcGeom& g) {
   w.inv = o; o = align256(o + (size_t)g.npix * 4);
   w.work = o; o = align256(o + (size_t)w.max_work * 16);
   w.work_count = o; o = align256(o + 4);
-  w.scratch = o; o = align256(o + (size_t)g.L * g.npix * g.RDP * 2);
+  w.scratch = o; o = align256(o + (size_t)g.L * g.npix * std::max(g.RDP, g.RDQ) * 2);
   w.total = o;
   return w;
+}
+
+struct TcWs {
+  int* counts;
+  int* offsets;
+  int2* keyrank;
+  int* sorted;
+  int* inv;
+  int4* work;
+  int* work_count;
+  __half* scratch;
+};
+
+TcWs ws_pointers(void* ws, const WsLayout& L) {
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  TcWs p;
+  p.counts = reinterpret_cast<int*>(w + L.counts);
+  p.offsets = reinterpret_cast<int*>(w + L.offsets);
+  p.keyrank = reinterpret_cast<int2*>(w + L.keyrank);
+  p.sorted = reinterpret_cast<int*>(w + L.sorted);
+  p.inv = reinterpret_cast<int*>(w + L.inv);
+  p.work = reinterpret_cast<int4*>(w + L.work);
+  p.work_count = reinterpret_cast<int*>(w + L.work_count);
+  p.scratch = reinterpret_cast<__half*>(w + L.scratch);
+  return p;
+}
+
+// Counting sort of the pixels into anchor cells + the chunk work list.
+bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStream_t s) {
+  if (cudaMemsetAsync(W.counts, 0, sizeof(int) * (size_t)g.B * g.ncell, s) != cudaSuccess)
+    return check_launch("memset counts");
+  const int threads = 256;
+  const int blocks = (int)((g.npix + threads - 1) / threads);
+  if (cdtype == LCB200_F32)
+    tc_hist_kernel<float><<<blocks, threads, 0, s>>>((const float*)co, W.counts, W.keyrank, g);
+  else
+    tc_hist_kernel<__half><<<blocks, threads, 0, s>>>((const __half*)co, W.counts, W.keyrank, g);
+  count_launch();
+  if (!check_launch("tc_hist")) return false;
+  tc_scan_kernel<<<1, 1024, 0, s>>>(W.counts, W.offsets, W.work, W.work_count, g.B * g.ncell,
+                                    g.ncell);
+  count_launch();
+  if (!check_launch("tc_scan")) return false;
+  tc_scatter_kernel<<<blocks, threads, 0, s>>>(W.keyrank, W.offsets, W.sorted, W.inv, g);
+  count_launch();
+  return check_launch("tc_scatter");
 }
 
 size_t fwd_smem_bytes(const TcGeom& g, int nstage, uint32_t* stage_bytes) {
@@ -605,32 +1298,13 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
     set_error("cuTensorMapEncodeTiled unavailable from the driver");
     return false;
   }
-  uint8_t* w = static_cast<uint8_t*>(ws);
-  int* counts = reinterpret_cast<int*>(w + L.counts);
-  int* offsets = reinterpret_cast<int*>(w + L.offsets);
-  int2* keyrank = reinterpret_cast<int2*>(w + L.keyrank);
-  int* sorted = reinterpret_cast<int*>(w + L.sorted);
-  int* inv = reinterpret_cast<int*>(w + L.inv);
-  int4* work = reinterpret_cast<int4*>(w + L.work);
-  int* work_count = reinterpret_cast<int*>(w + L.work_count);
-  __half* scratch = reinterpret_cast<__half*>(w + L.scratch);
-
-  if (cudaMemsetAsync(counts, 0, sizeof(int) * (size_t)B * g.ncell, s) != cudaSuccess)
-    return check_launch("memset counts");
-  const int threads = 256;
-  const int blocks = (int)((g.npix + threads - 1) / threads);
-  if (cdtype == LCB200_F32)
-    tc_hist_kernel<float><<<blocks, threads, 0, s>>>((const float*)co, counts, keyrank, g);
-  else
-    tc_hist_kernel<__half><<<blocks, threads, 0, s>>>((const __half*)co, counts, keyrank, g);
-  count_launch();
-  if (!check_launch("tc_hist")) return false;
-  tc_scan_kernel<<<1, 1024, 0, s>>>(counts, offsets, work, work_count, B * g.ncell, g.ncell);
-  count_launch();
-  if (!check_launch("tc_scan")) return false;
-  tc_scatter_kernel<<<blocks, threads, 0, s>>>(keyrank, offsets, sorted, inv, g);
-  count_launch();
-  if (!check_launch("tc_scatter")) return false;
+  TcWs W = ws_pointers(ws, L);
+  if (!tc_sort(W, g, co, cdtype, s)) return false;
+  int* sorted = W.sorted;
+  int* inv = W.inv;
+  int4* work = W.work;
+  int* work_count = W.work_count;
+  __half* scratch = W.scratch;
 
   TcFwdParams prm;
   memset(&prm, 0, sizeof(prm));
@@ -677,15 +1351,133 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
   return check_launch("tc_unsort");
 }
 
-bool tc_bwd_eligible(int, int, int, int, int, int, int, int, std::string* why) {
-  if (why) *why = "tensor-core backward not built";
-  return false;
+namespace {
+
+size_t bwd1_stage_bytes(const TcGeom& g) { return 16384 + (size_t)g.KC * 8192; }
+size_t bwd2_stage_bytes(const TcGeom& g) { return 32768 + (size_t)g.KC * 16384; }
+
+int pick_stages(size_t stage, size_t extra, int maxst) {
+  const size_t lim = (size_t)max_dyn_smem();
+  int n = maxst;
+  while (n >= 2 && 1024 + n * stage + extra > lim) --n;
+  return n;
 }
 
-bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int, int,
-                 int, int, int, int, int, bool, float, void*, size_t, cudaStream_t) {
-  set_error("tensor-core backward not built");
-  return false;
+bool bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation, int dtype,
+                  std::string* why, TcGeom* out, int* nst1, int* nst2) {
+  TcGeom g;
+  int nf = 0;
+  if (!eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, &g, &nf)) return false;
+  if (g.RDQ == 0) return false;
+  const int n1 = pick_stages(bwd1_stage_bytes(g), 256, 4);
+  const int n2 = pick_stages(bwd2_stage_bytes(g), 256, 2);
+  if (n1 < 2 || n2 < 2) {
+    if (why) *why = "tensor-core backward shared-memory budget exceeded";
+    return false;
+  }
+  if (out) *out = g;
+  if (nst1) *nst1 = n1;
+  if (nst2) *nst2 = n2;
+  return true;
+}
+
+template <int RADIUS>
+bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __half* corr_grad,
+                        const int* inv, __half* gint, float scale, int ymajor, cudaStream_t s) {
+  const TcGeom& g = p1.g;
+  dim3 ug((g.HW + 127) / 128, g.L, g.B);
+  tc_gint_kernel<RADIUS><<<ug, 128, 0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gint,
+                                            p1.grad_f1, scale, ymajor, g);
+  count_launch();
+  if (!check_launch("tc_gint")) return false;
+  const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256;
+  auto k1 = tc_bwd1_kernel<RADIUS>;
+  if (!ensure_smem_attr((const void*)k1, smem1)) return false;
+  k1<<<num_sms(), kFwdThreads, smem1, s>>>(p1);
+  count_launch();
+  if (!check_launch("tc_bwd1")) return false;
+  const size_t smem2 = std::max<size_t>(1024 + (size_t)p2.nstage * p2.stage_bytes + 256, 120 * 1024);
+  auto k2 = tc_bwd2_kernel<RADIUS>;
+  if (!ensure_smem_attr((const void*)k2, smem2)) return false;
+  k2<<<num_sms(), kBwd2Threads, smem2, s>>>(p2);
+  count_launch();
+  return check_launch("tc_bwd2");
+}
+
+}  // namespace
+
+bool tc_bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
+                     int dtype, std::string* why) {
+  return bwd_eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, nullptr, nullptr,
+                      nullptr);
+}
+
+bool tc_backward(const void* f1, const void* f2, const void* co, const void* gout, void* f1g,
+                 float* f2g, int B, int H1, int W1, int C, int radius, int levels, int cdtype,
+                 bool ymajor, float scale, void* ws, size_t ws_bytes, cudaStream_t s) {
+  TcGeom g;
+  int n1 = 0, n2 = 0;
+  std::string why;
+  if (!bwd_eligible(B, H1, W1, C, radius, levels, 1, LCB200_F16, &why, &g, &n1, &n2)) {
+    set_error("tensor-core backward: " + why);
+    return false;
+  }
+  const WsLayout L = ws_layout(g);
+  if (ws_bytes < L.total) {
+    set_error("tensor-core backward: workspace too small");
+    return false;
+  }
+  auto encode = get_encode_fn();
+  if (!encode) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return false;
+  }
+  TcWs W = ws_pointers(ws, L);
+  if (!tc_sort(W, g, co, cdtype, s)) return false;
+
+  TcBwdParams p1;
+  memset(&p1, 0, sizeof(p1));
+  for (int l = 0; l < levels; ++l) {
+    const __half* base = static_cast<const __half*>(f2) + g.off[l];
+    cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)g.w[l], (cuuint64_t)g.h[l], (cuuint64_t)B};
+    cuuint64_t strides[3] = {(cuuint64_t)C * 2, (cuuint64_t)g.w[l] * C * 2,
+                             (cuuint64_t)g.batch_elems * 2};
+    cuuint32_t box[4] = {64, (cuuint32_t)g.UW[l], (cuuint32_t)g.Rg[l], 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = encode(&p1.tmap[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, (void*)base, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled failed for level " + std::to_string(l));
+      return false;
+    }
+  }
+  p1.coords = co;
+  p1.coords_f32 = cdtype == LCB200_F32;
+  p1.sorted = W.sorted;
+  p1.counts = W.counts;
+  p1.offsets = W.offsets;
+  p1.work = W.work;
+  p1.work_count = W.work_count;
+  p1.gint = W.scratch;
+  p1.fmap1 = static_cast<const __half*>(f1);
+  p1.grad_f1 = static_cast<__half*>(f1g);
+  p1.grad_f2 = f2g;
+  p1.g = g;
+  p1.nitems = g.items_before[levels];
+  TcBwdParams p2 = p1;
+  p1.nstage = n1;
+  p1.stage_bytes = (uint32_t)bwd1_stage_bytes(g);
+  p2.nstage = n2;
+  p2.stage_bytes = (uint32_t)bwd2_stage_bytes(g);
+  const __half* cg = static_cast<const __half*>(gout);
+  switch (radius) {
+    case 3: return launch_bwd_kernels<3>(p1, p2, cg, W.inv, W.scratch, scale, ymajor, s);
+    case 4: return launch_bwd_kernels<4>(p1, p2, cg, W.inv, W.scratch, scale, ymajor, s);
+    case 8: return launch_bwd_kernels<8>(p1, p2, cg, W.inv, W.scratch, scale, ymajor, s);
+    default: set_error("radius not instantiated"); return false;
+  }
 }
 
 int tc_device_status(bool reset) {

@@ -145,3 +145,76 @@ def test_tc_config2_shape_spot_check():
     simt = ops.pyramid_corr_forward(fm1, packed, co16.to(DEV), r, levels, 1, False, 1.0 / 16,
                                     _lib.ENGINE_SIMT)
     torch.testing.assert_close(out.float(), simt.float(), rtol=2e-3, atol=2e-3)
+
+
+BWD_CASES = [
+    (2, 256, 40, 52, 4, 4, "gauss_oob"),
+    (1, 128, 33, 70, 4, 3, "smooth"),
+    (1, 128, 30, 40, 4, 8, "uniform64"),
+    (1, 64, 24, 36, 2, 4, "uniform8"),
+    (1, 256, 24, 40, 3, 3, "converge"),
+]
+
+
+@pytest.mark.parametrize("case", BWD_CASES, ids=lambda c: "b{}c{}_{}x{}_l{}r{}_{}".format(*c))
+def test_tc_backward_vs_oracle_and_simt(case):
+    b, c, h, w, levels, r, kind = case
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, kind, seed=11)
+    co16 = co.half()
+    rd = 2 * r + 1
+    scale = 1.0 / math.sqrt(c)
+    gout = torch.randn(b, levels, rd * rd, h, w, generator=torch.Generator().manual_seed(4)).half()
+    g1, g2 = ops.pyramid_corr_backward(fm1, packed, co16.to(DEV), gout.to(DEV), r, levels, 1,
+                                       False, scale, _lib.ENGINE_TC)
+    s1, s2 = ops.pyramid_corr_backward(fm1, packed, co16.to(DEV), gout.to(DEV), r, levels, 1,
+                                       False, scale, _lib.ENGINE_SIMT)
+    torch.testing.assert_close(g1.float(), s1.float(), rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(g2, s2, rtol=1e-2, atol=1e-2)
+    # oracle: gradients of the (scaled) pyramid correlation w.r.t. the NHWC
+    # fmap1 and the NCHW fmap2 (through the pyramid build's gradient)
+    x1 = f1.double().requires_grad_(True)
+    x2 = f2.double().requires_grad_(True)
+    o = oracle.pyramid_corr(x1, x2, co16.double(), levels, r) * scale
+    e1, e2 = torch.autograd.grad(o, [x1, x2], gout.double())
+    torch.testing.assert_close(g1.permute(0, 3, 1, 2).double().cpu(), e1, **F16TOL)
+    g2n = ops.pyramid_build_backward(g2, (b, c, h, w), levels, torch.float32)
+    torch.testing.assert_close(g2n.double().cpu(), e2, rtol=1e-2, atol=1e-2)
+
+
+def test_tc_backward_accumulates_into_reference_buffer():
+    # launchLocalCorrCudaPyramidBackward adds into the caller's float32 buffer.
+    import localcorr_b200 as lc
+
+    b, c, h, w, levels, r = 1, 128, 30, 44, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "gauss_oob", seed=12)
+    fm1 = fm1.requires_grad_(True)
+    packed = packed.requires_grad_(True)
+    out = lc.LocalCorrCudaPyramidFunction.apply(fm1, packed, co.half().to(DEV), r, levels, 1,
+                                                False)
+    g = torch.randn(out.shape, generator=torch.Generator().manual_seed(5)).half().to(DEV)
+    a1, a2 = torch.autograd.grad(out, [fm1, packed], g)
+    s1, s2 = ops.pyramid_corr_backward(fm1.detach(), packed.detach(), co.half().to(DEV), g, r,
+                                       levels, 1, False, 1.0, _lib.ENGINE_SIMT)
+    torch.testing.assert_close(a1.float(), s1.float(), rtol=1e-2, atol=2e-2)
+    torch.testing.assert_close(a2.float(), s2.half().float(), rtol=1e-2, atol=2e-2)
+
+
+def test_tc_backward_config2_shape_adjoint():
+    # <grad_f1, d1> == <g, corr(d1, f2)> and <grad_f2, d2> == <g, corr(f1, d2)>
+    # at the full configuration-2 image size (one image), float16 engine.
+    b, c, h, w, levels, r = 1, 256, 135, 240, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "gauss_oob", seed=13)
+    co16 = co.half().to(DEV)
+    g = (torch.randn(b, levels, 81, h, w, generator=torch.Generator().manual_seed(6)) * 0.25).half().to(DEV)
+    g1, g2 = ops.pyramid_corr_backward(fm1, packed, co16, g, r, levels, 1, False, 1.0 / 16,
+                                       _lib.ENGINE_TC)
+    d1 = (torch.randn(fm1.shape, generator=torch.Generator().manual_seed(7)) * 0.5).half().to(DEV)
+    d2 = (torch.randn(packed.shape, generator=torch.Generator().manual_seed(8)) * 0.5).half().to(DEV)
+    c1 = ops.pyramid_corr_forward(d1, packed, co16, r, levels, 1, False, 1.0 / 16, _lib.ENGINE_TC)
+    c2 = ops.pyramid_corr_forward(fm1, d2, co16, r, levels, 1, False, 1.0 / 16, _lib.ENGINE_TC)
+    lhs1 = (g1.double() * d1.double()).sum().item()
+    rhs1 = (g.double() * c1.double()).sum().item()
+    lhs2 = (g2.double() * d2.double()).sum().item()
+    rhs2 = (g.double() * c2.double()).sum().item()
+    assert abs(lhs1 - rhs1) <= 2e-3 * (abs(rhs1) + (g.double().norm() * c1.double().norm()).item() * 1e-2)
+    assert abs(lhs2 - rhs2) <= 2e-3 * (abs(rhs2) + (g.double().norm() * c2.double().norm()).item() * 1e-2)

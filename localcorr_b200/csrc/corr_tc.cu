@@ -513,7 +513,8 @@ template <int RADIUS>
 __global__ void __launch_bounds__(128)
 tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
                int coords_f32, const int* __restrict__ inv, __half* __restrict__ gint,
-               __half* __restrict__ grad_f1, float scale, int ymajor, TcGeom g) {
+               int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale, int ymajor,
+               TcGeom g) {
   constexpr int RD = 2 * RADIUS + 1;
   constexpr int NG = RD + 1;
   const int pix = blockIdx.x * blockDim.x + threadIdx.x;
@@ -540,6 +541,10 @@ tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ co
   const float inv_s = 1.f / (float)(1 << l);
   const float clx = cx * inv_s, cly = cy * inv_s;
   const float dx = clx - floorf(clx), dy = cly - floorf(cly);
+  // Level-l integer base of the window, packed (x low, y high, int16 each),
+  // in sorted order: the grad_fmap2 pull reads it coalesced per candidate.
+  sbase[(long long)l * g.npix + idx] =
+      ((int)floorf(clx) & 0xFFFF) | ((int)floorf(cly) << 16);
   const float wa = (1.f - dx) * (1.f - dy) * scale, wb = dx * (1.f - dy) * scale;
   const float wc = (1.f - dx) * dy * scale, wd = dx * dy * scale;
   const __half* src = corr_grad + ((long long)b * g.L + l) * RD * RD * g.HW + pix;
@@ -579,6 +584,7 @@ struct alignas(64) TcBwdParams {
   const int4* work;
   const int* work_count;
   const __half* gint;
+  const int* sbase;
   const __half* fmap1;
   __half* grad_f1;
   float* grad_f2;
@@ -747,7 +753,17 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_co
         const int rx = (int)floorf(cx * inv) - (cell_x0 >> l);
         const int ry = (int)floorf(cy * inv) - (cell_y0 >> l);
         const int UW = g.UW[l], Rg = g.Rg[l];
-        const __half* grow = p.gint + ((long long)l * g.npix + idx) * g.RDQ;
+        // This pixel's gint row -> per-thread shared scratch (global loads
+        // batched ahead of the shared stores).
+        __half* grow = reinterpret_cast<__half*>(smem + (size_t)NST * SB + 256) + (size_t)t * g.RDQ;
+        if (valid) {
+          const uint4* src = reinterpret_cast<const uint4*>(p.gint + ((long long)l * g.npix + idx) * g.RDQ);
+          uint4 tmp[(NG * NG + 7) / 8];
+#pragma unroll
+          for (int i = 0; i < (NG * NG + 7) / 8; ++i) tmp[i] = src[i];
+#pragma unroll
+          for (int i = 0; i < (NG * NG + 7) / 8; ++i) reinterpret_cast<uint4*>(grow)[i] = tmp[i];
+        }
         for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
           const int s = gs % NST;
           const uint32_t use = gs / NST;
@@ -860,7 +876,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   constexpr int NG = RD + 1;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
-  __shared__ int wcount[4];
+  __shared__ int item_rows;        // rows allocated in the current item
   __shared__ int stage_flags[8];   // bit0: last stage of the item, bit1: item has pixels
   const TcGeom& g = p.g;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -920,6 +936,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           if (!tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
           tc::tc_fence_after();
           const int flags = stage_flags[s];
+          stage_flags[s] = 0;
           const uint32_t sa = base + s * SB;
           const uint32_t sb = sa + 32768;
 #pragma unroll
@@ -942,9 +959,15 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     __syncwarp();
   } else if (warp <= 4) {
     // ---------------- builders ----------------
+    // Kept (pixel, Q) pairs get consecutive rows of the item through one
+    // shared counter; row r of the item goes to stage item_first + r/128.
+    // Each row writer arrives once on its stage's afull barrier; at the end
+    // of the item the rows of the closing stage past the last kept pixel
+    // are zeroed and arrive too, so every stage sees exactly 128 arrivals.
     const int bw = warp - 1;          // builder warp 0..3
     const int bt = bw * 32 + lane;    // builder thread 0..127
-    uint32_t gs = 0, bphase = 0;
+    uint8_t* scr = smem + (size_t)NST * SB + 512 + (size_t)bt * g.RDQ * 2;
+    uint32_t gs0 = 0, bphase = 0;
     bool ok = true;
     auto bsync = [&]() -> bool {
       tc::mbar_arrive(bsync_bar);
@@ -953,114 +976,107 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     const unsigned lt_mask = (1u << lane) - 1u;
     for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
       const Bwd2Item item = decode_item(g, it, RADIUS);
-      const int l = item.l, b = item.b;
+      const int l = item.l;
       const int hl = g.h[l], wl = g.w[l];
-      const float inv = 1.f / (float)(1 << l);
-      int fill = 0;        // rows used in the current stage (uniform)
-      bool any = false;    // item has at least one pixel (uniform)
-      int s = gs % NST;
-      if (!tc::mbar_wait(empty + s, ((gs / NST) & 1) ^ 1, abort)) { ok = false; break; }
+      if (bt == 0) item_rows = 0;
+      if (!bsync()) { ok = false; break; }
+      const int* sb_l = p.sbase + (long long)l * g.npix;
       for (int cyr = item.ra; cyr <= item.rb && ok && !item.empty; ++cyr) {
-        const long long c0 = (long long)b * g.ncell + (long long)cyr * g.ncx + item.ca;
-        const long long c1 = (long long)b * g.ncell + (long long)cyr * g.ncx + item.cb;
+        const long long c0 = (long long)item.b * g.ncell + (long long)cyr * g.ncx + item.ca;
+        const long long c1 = (long long)item.b * g.ncell + (long long)cyr * g.ncx + item.cb;
         const int s0 = p.offsets[c0];
         const int s1 = p.offsets[c1] + p.counts[c1];
-        for (int base = s0; base < s1 && ok; base += kTile) {
+        for (int base = s0; base < s1; base += kTile) {
           const int pos = base + bt;
           bool touch = false;
-          int gid = 0, x0 = 0, y0 = 0;
+          int x0 = 0, y0 = 0, ylo = 0, yhi = -1, xlo = 0, xhi = -1;
           if (pos < s1) {
-            gid = p.sorted[pos];
-            float cx, cy;
-            pixel_coords(p, b, gid - b * g.HW, cx, cy);
-            x0 = (int)floorf(cx * inv);
-            y0 = (int)floorf(cy * inv);
-            // window rows y0-r..y0+r+1 meet Q rows qy0..qy0+7 (and the map)
-            const int ylo = max(max(y0 - RADIUS, item.qy0), 0);
-            const int yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
-            const int xlo = max(max(x0 - RADIUS, item.qx0), 0);
-            const int xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
+            const int pk = sb_l[pos];
+            x0 = (int)(short)(pk & 0xFFFF);
+            y0 = pk >> 16;
+            ylo = max(max(y0 - RADIUS, item.qy0), 0);
+            yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
+            xlo = max(max(x0 - RADIUS, item.qx0), 0);
+            xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
             touch = ylo <= yhi && xlo <= xhi;
           }
           const unsigned ballot = __ballot_sync(0xffffffffu, touch);
-          if (lane == 0) wcount[bw] = __popc(ballot);
-          if (!bsync()) { ok = false; break; }
-          int woff = 0, total = 0;
+          if (ballot == 0) continue;
+          int first = 0;
+          if (lane == 0) first = atomicAdd(&item_rows, __popc(ballot));
+          first = __shfl_sync(0xffffffffu, first, 0);
+          if (!touch) continue;
+          // gint row of this pixel -> per-thread scratch (global loads
+          // batched ahead of the shared stores)
+          const uint4* grow = reinterpret_cast<const uint4*>(
+              p.gint + ((long long)l * g.npix + pos) * g.RDQ);
+          const int gid = p.sorted[pos];
+          {
+            uint4 tmp[(NG * NG + 7) / 8];
 #pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const int c = wcount[w];
-            woff += (w < bw) ? c : 0;
-            total += c;
+            for (int i = 0; i < (NG * NG + 7) / 8; ++i) tmp[i] = grow[i];
+#pragma unroll
+            for (int i = 0; i < (NG * NG + 7) / 8; ++i) reinterpret_cast<uint4*>(scr)[i] = tmp[i];
           }
-          if (!bsync()) { ok = false; break; }
-          if (total == 0) continue;
-          any = true;
-          const int slot = fill + woff + __popc(ballot & lt_mask);
-          // Rows that fit the current stage, then the overflow into the next.
-          auto write_row = [&](int st, int row) {
-            uint8_t* A = smem + (size_t)st * SB;
-            uint8_t* Bm = A + 32768;
-            // A row: this pixel's G restricted to Q (position = 16*dy + dx)
+          const int r = first + __popc(ballot & lt_mask);
+          const uint32_t st = gs0 + (uint32_t)(r / kTile);
+          const int row = r % kTile;
+          const int s = st % NST;
+          if (!tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort)) { ok = false; continue; }
+          uint8_t* A = smem + (size_t)s * SB;
+          uint8_t* Bm = A + 32768;
+          const __half* f1 = p.fmap1 + (long long)gid * g.C;
+          for (int kc = 0; kc < g.KC; ++kc)
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
+            for (int j = 0; j < 8; ++j)
+              tc::cp_async_16(Bm + kc * 16384 + row * 128 + ((j ^ (row & 7)) << 4),
+                              f1 + kc * 64 + j * 8, 16);
 #pragma unroll
-              for (int j = 0; j < 8; ++j)
-                *reinterpret_cast<uint4*>(A + m * 16384 + row * 128 + (j << 4)) = make_uint4(0, 0, 0, 0);
-            const __half* grow = p.gint + ((long long)l * g.npix + pos) * g.RDQ;
-            const int ylo = max(max(y0 - RADIUS, item.qy0), 0);
-            const int yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
-            const int xlo = max(max(x0 - RADIUS, item.qx0), 0);
-            const int xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
-            for (int yy = ylo; yy <= yhi; ++yy) {
-              for (int xx = xlo; xx <= xhi; ++xx) {
-                const int pq = (yy - item.qy0) * 16 + (xx - item.qx0);
-                const int m = pq >> 6, cc = pq & 63;
-                *reinterpret_cast<__half*>(A + m * 16384 + row * 128 + ((((cc >> 3) ^ (row & 7))) << 4) +
-                                           (cc & 7) * 2) =
-                    grow[(yy - (y0 - RADIUS)) * NG + (xx - (x0 - RADIUS))];
-              }
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(A + m * 16384 + row * 128 + (j << 4)) = make_uint4(0, 0, 0, 0);
+          const __half* gsm = reinterpret_cast<const __half*>(scr);
+          for (int yy = ylo; yy <= yhi; ++yy) {
+            const int jrow = (yy - (y0 - RADIUS)) * NG - (x0 - RADIUS);
+            const int prow = (yy - item.qy0) * 16 - item.qx0;
+            for (int xx = xlo; xx <= xhi; ++xx) {
+              const int pq = prow + xx;
+              const int m = pq >> 6, cc = pq & 63;
+              *reinterpret_cast<__half*>(A + m * 16384 + row * 128 +
+                                         ((((cc >> 3) ^ (row & 7))) << 4) + (cc & 7) * 2) =
+                  gsm[jrow + xx];
             }
-            // B row: the pixel's fmap1 row, 64-channel blocks
-            const __half* f1 = p.fmap1 + (long long)gid * g.C;
-            for (int kc = 0; kc < g.KC; ++kc)
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                tc::cp_async_16(Bm + kc * 16384 + row * 128 + ((j ^ (row & 7)) << 4),
-                                f1 + kc * 64 + j * 8, 16);
-          };
-          if (touch && slot < kTile) write_row(s, slot);
-          if (fill + total >= kTile) {
-            // current stage complete: publish it
-            tc::cp_async_wait_all();
-            tc::fence_proxy_async_smem();
-            if (bt == 0) stage_flags[s] = 2;  // not last, item has pixels
-            tc::mbar_arrive(afull + s);
-            ++gs;
-            s = gs % NST;
-            if (!tc::mbar_wait(empty + s, ((gs / NST) & 1) ^ 1, abort)) { ok = false; break; }
-            if (touch && slot >= kTile) write_row(s, slot - kTile);
-            fill = fill + total - kTile;
-          } else {
-            fill += total;
           }
+          tc::cp_async_wait_all();
+          tc::fence_proxy_async_smem();
+          tc::mbar_arrive(afull + s);
         }
       }
       if (!ok) break;
-      // Close the item: zero the unused rows of the current stage (A only;
-      // stale B rows are finite and meet zero weights), flag it last.
+      // Close the item.
+      if (!bsync()) { ok = false; break; }
+      const int T = item_rows;
+      const uint32_t cs = gs0 + (uint32_t)(T / kTile);
+      const int fill = T % kTile;
+      const int s = cs % NST;
+      if (bt == 0) {
+        if (!tc::mbar_wait(empty + s, ((cs / NST) & 1) ^ 1, abort)) ok = false;
+        else stage_flags[s] = 1 | (T > 0 ? 2 : 0);
+      }
+      if (!bsync() || !ok) { ok = false; break; }
       if (bt >= fill) {
+        if (!tc::mbar_wait(empty + s, ((cs / NST) & 1) ^ 1, abort)) { ok = false; break; }
         uint8_t* A = smem + (size_t)s * SB;
 #pragma unroll
         for (int m = 0; m < 2; ++m)
 #pragma unroll
           for (int j = 0; j < 8; ++j)
             *reinterpret_cast<uint4*>(A + m * 16384 + bt * 128 + (j << 4)) = make_uint4(0, 0, 0, 0);
+        tc::fence_proxy_async_smem();
+        tc::mbar_arrive(afull + s);
       }
-      tc::cp_async_wait_all();
-      tc::fence_proxy_async_smem();
-      if (bt == 0) stage_flags[s] = 1 | (any ? 2 : 0);
-      tc::mbar_arrive(afull + s);
-      ++gs;
+      gs0 = cs + 1;
     }
   } else {
     // ---------------- epilogue ----------------
@@ -1153,7 +1169,7 @@ int num_sms() {
 }
 
 struct WsLayout {
-  size_t counts, offsets, keyrank, sorted, inv, work, work_count, scratch, total;
+  size_t counts, offsets, keyrank, sorted, inv, work, work_count, sbase, scratch, total;
   long long max_work;
 };
 
@@ -1171,6 +1187,7 @@ WsLayout ws_layout(const TcGeom& g) {
   w.inv = o; o = align256(o + (size_t)g.npix * 4);
   w.work = o; o = align256(o + (size_t)w.max_work * 16);
   w.work_count = o; o = align256(o + 4);
+  w.sbase = o; o = align256(o + (size_t)g.L * g.npix * 4);
   w.scratch = o; o = align256(o + (size_t)g.L * g.npix * std::max(g.RDP, g.RDQ) * 2);
   w.total = o;
   return w;
@@ -1184,6 +1201,7 @@ struct TcWs {
   int* inv;
   int4* work;
   int* work_count;
+  int* sbase;
   __half* scratch;
 };
 
@@ -1197,6 +1215,7 @@ TcWs ws_pointers(void* ws, const WsLayout& L) {
   p.inv = reinterpret_cast<int*>(w + L.inv);
   p.work = reinterpret_cast<int4*>(w + L.work);
   p.work_count = reinterpret_cast<int*>(w + L.work_count);
+  p.sbase = reinterpret_cast<int*>(w + L.sbase);
   p.scratch = reinterpret_cast<__half*>(w + L.scratch);
   return p;
 }
@@ -1369,8 +1388,8 @@ bool bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dila
   int nf = 0;
   if (!eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, &g, &nf)) return false;
   if (g.RDQ == 0) return false;
-  const int n1 = pick_stages(bwd1_stage_bytes(g), 256, 4);
-  const int n2 = pick_stages(bwd2_stage_bytes(g), 256, 2);
+  const int n1 = pick_stages(bwd1_stage_bytes(g), 256 + (size_t)kTile * g.RDQ * 2, 4);
+  const int n2 = pick_stages(bwd2_stage_bytes(g), 512 + (size_t)kTile * g.RDQ * 2, 2);
   if (n1 < 2 || n2 < 2) {
     if (why) *why = "tensor-core backward shared-memory budget exceeded";
     return false;
@@ -1387,16 +1406,18 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
   const TcGeom& g = p1.g;
   dim3 ug((g.HW + 127) / 128, g.L, g.B);
   tc_gint_kernel<RADIUS><<<ug, 128, 0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gint,
-                                            p1.grad_f1, scale, ymajor, g);
+                                            const_cast<int*>(p1.sbase), p1.grad_f1, scale,
+                                            ymajor, g);
   count_launch();
   if (!check_launch("tc_gint")) return false;
-  const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256;
+  const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256 + (size_t)kTile * g.RDQ * 2;
   auto k1 = tc_bwd1_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k1, smem1)) return false;
   k1<<<num_sms(), kFwdThreads, smem1, s>>>(p1);
   count_launch();
   if (!check_launch("tc_bwd1")) return false;
-  const size_t smem2 = std::max<size_t>(1024 + (size_t)p2.nstage * p2.stage_bytes + 256, 120 * 1024);
+  const size_t smem2 = std::max<size_t>(
+      1024 + (size_t)p2.nstage * p2.stage_bytes + 512 + (size_t)kTile * g.RDQ * 2, 120 * 1024);
   auto k2 = tc_bwd2_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k2, smem2)) return false;
   k2<<<num_sms(), kBwd2Threads, smem2, s>>>(p2);
@@ -1461,6 +1482,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.work = W.work;
   p1.work_count = W.work_count;
   p1.gint = W.scratch;
+  p1.sbase = W.sbase;
   p1.fmap1 = static_cast<const __half*>(f1);
   p1.grad_f1 = static_cast<__half*>(f1g);
   p1.grad_f2 = f2g;

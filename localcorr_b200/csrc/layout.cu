@@ -50,10 +50,13 @@ template <typename T, int CC>
 __global__ void __launch_bounds__(256)
 pyramid_build_kernel(const T* __restrict__ in, T* __restrict__ packed, int C, int H,
                      int W, PyrGeom g, int nlev) {
-  // s[l] holds level l of the tile, channel-major [CC][ty][tx], fp32 values
-  // equal to the dtype-rounded level values.
-  __shared__ float s0[CC * kTY * kTX];
-  __shared__ float s1[CC * (kTY / 2) * (kTX / 2)];
+  // s[l] holds level l of the tile as [ty][tx][CC+1] (one padding word per
+  // pixel keeps both the x-fastest NCHW side and the channel-fastest NHWC
+  // side free of bank conflicts), fp32 values equal to the dtype-rounded
+  // level values.
+  constexpr int CP = CC + 1;
+  __shared__ float s0[kTY * kTX * CP];
+  __shared__ float s1[(kTY / 2) * (kTX / 2) * CP];
   const int b = blockIdx.z;
   const int c0 = blockIdx.y * CC;
   const int tiles_x = (W + kTX - 1) / kTX;
@@ -70,7 +73,7 @@ pyramid_build_kernel(const T* __restrict__ in, T* __restrict__ packed, int C, in
     float v = 0.f;
     if (c < nc && gy < H && gx < W)
       v = ldf(in + (((long long)b * C + c0 + c) * H + gy) * W + gx);
-    s0[i] = v;
+    s0[(y * kTX + x) * CP + c] = v;
   }
   __syncthreads();
 
@@ -82,7 +85,7 @@ pyramid_build_kernel(const T* __restrict__ in, T* __restrict__ packed, int C, in
     const int y = i / (CC * kTX);
     const int gy = ty0 + y, gx = tx0 + x;
     if (c < nc && gy < H && gx < W)
-      stf(pb + g.off[0] + ((long long)gy * W + gx) * C + c0 + c, s0[(c * kTY + y) * kTX + x]);
+      stf(pb + g.off[0] + ((long long)gy * W + gx) * C + c0 + c, s0[(y * kTX + x) * CP + c]);
   }
 
   float* src = s0;
@@ -92,16 +95,16 @@ pyramid_build_kernel(const T* __restrict__ in, T* __restrict__ packed, int C, in
     const int ny = sy / 2, nx = sx / 2;
     __syncthreads();
     for (int i = threadIdx.x; i < CC * ny * nx; i += blockDim.x) {
-      const int x = i % nx;
-      const int y = (i / nx) % ny;
-      const int c = i / (nx * ny);
-      const float* q = src + (c * sy + 2 * y) * sx + 2 * x;
+      const int c = i % CC;
+      const int x = (i / CC) % nx;
+      const int y = i / (CC * nx);
+      const float* q = src + ((2 * y) * sx + 2 * x) * CP + c;
       float acc = q[0];
-      acc += q[1];
-      acc += q[sx];
-      acc += q[sx + 1];
+      acc += q[CP];
+      acc += q[sx * CP];
+      acc += q[sx * CP + CP];
       // Round to the storage dtype so the next level pools rounded values.
-      dst[i] = Elem<T>::to_f(Elem<T>::from_f(acc / 4.f));
+      dst[(y * nx + x) * CP + c] = Elem<T>::to_f(Elem<T>::from_f(acc / 4.f));
     }
     __syncthreads();
     const int hl = g.h[l], wl = g.w[l];
@@ -112,7 +115,7 @@ pyramid_build_kernel(const T* __restrict__ in, T* __restrict__ packed, int C, in
       const int y = i / (CC * nx);
       const int gy = oy + y, gx = ox + x;
       if (c < nc && gy < hl && gx < wl)
-        stf(pb + g.off[l] + ((long long)gy * wl + gx) * C + c0 + c, dst[(c * ny + y) * nx + x]);
+        stf(pb + g.off[l] + ((long long)gy * wl + gx) * C + c0 + c, dst[(y * nx + x) * CP + c]);
     }
     // Ping-pong: level l becomes the source of level l+1. s0 is free after
     // level 1 has been computed from it, so levels alternate s1 -> s0 -> s1.
@@ -152,7 +155,8 @@ template <typename T, typename G, int CC>
 __global__ void __launch_bounds__(256)
 pyramid_grad_kernel(const G* __restrict__ gp, T* __restrict__ out, int C, int H, int W,
                     PyrGeom g) {
-  __shared__ float acc[CC * kTY * kTX];
+  constexpr int CP = CC + 1;  // [ty][tx][CC+1]: conflict-free on both sides
+  __shared__ float acc[kTY * kTX * CP];
   const int b = blockIdx.z;
   const int c0 = blockIdx.y * CC;
   const int tiles_x = (W + kTX - 1) / kTX;
@@ -175,7 +179,7 @@ pyramid_grad_kernel(const G* __restrict__ gp, T* __restrict__ out, int C, int H,
         sc *= 0.25f;
       }
     }
-    acc[(c * kTY + y) * kTX + x] = v;
+    acc[(y * kTX + x) * CP + c] = v;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < CC * kTY * kTX; i += blockDim.x) {
@@ -184,7 +188,7 @@ pyramid_grad_kernel(const G* __restrict__ gp, T* __restrict__ out, int C, int H,
     const int c = i / (kTX * kTY);
     const int gy = ty0 + y, gx = tx0 + x;
     if (c < nc && gy < H && gx < W)
-      stf(out + (((long long)b * C + c0 + c) * H + gy) * W + gx, acc[i]);
+      stf(out + (((long long)b * C + c0 + c) * H + gy) * W + gx, acc[(y * kTX + x) * CP + c]);
   }
 }
 

@@ -108,6 +108,31 @@ LCB200_API bool launchLocalCorrB200PyramidBackward(
     int dtype, int coords_dtype, bool ymajor, float scale, bool accumulate, int engine,
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* ---- Allocation-free forward (no counterpart in the reference) -------------
+ * Some callers may not allocate device memory at the time they run the
+ * correlation: a TensorRT plugin's enqueue (the engine's memory is fixed when
+ * it is built), code recorded while a CUDA graph is being captured, or a
+ * serving runtime that reserves all of its memory at start-up. This entry
+ * point computes the same result as launchLocalCorrB200PyramidForward with
+ * the tensor-core engine, but takes its scratch from a fixed array that the
+ * library holds on every GPU that loads it (LCB200_NOALLOC_SCRATCH_BYTES, kept
+ * until the process exits) instead of from the caller or an allocator; it
+ * calls no cudaMalloc/cudaFree.
+ *  - Only tensor-core configurations: float16 maps, dilation 1, 1..4 levels,
+ *    C in {64,128,192,256}, radius in {3,4,8}; coords float16 or float32.
+ *  - Problems whose scratch (localCorrB200PyramidWorkspaceBytes) exceeds
+ *    LCB200_NOALLOC_SCRATCH_BYTES are rejected (false, message says so).
+ *  - The first call on a device looks up the array's device address; make
+ *    that first call before any stream capture.
+ *  - All calls on a device share the one array: calls that can overlap on
+ *    the GPU (different streams, no ordering) race and must be serialised by
+ *    the caller. Each call starts from a cleared state (no carry-over). */
+#define LCB200_NOALLOC_SCRATCH_BYTES (32ull << 20)
+LCB200_API bool launchLocalCorrB200PyramidForwardNoAlloc(
+    const void* fmap1, const void* fmap2_packed, const void* coords, void* corr,
+    int B, int H1, int W1, int C, int radius, int levels,
+    int dtype, int coords_dtype, bool ymajor, float scale, cudaStream_t stream);
+
 /* ---- Layout preparation (replaces the torch permute/avg_pool2d/cat chain of
  * LocalCorrCudaPyramidBlock.__init__, blocks.py:369-383) ------------------- */
 

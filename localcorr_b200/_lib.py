@@ -52,6 +52,10 @@ PROTOTYPES = {
         + [_c_int] * 7
         + [_c_int, _c_int, _c_bool, _c_float, _c_bool, _c_int, _c_void_p, _c_size_t, _c_void_p],
     ),
+    "launchLocalCorrB200PyramidForwardNoAlloc": (
+        _c_bool,
+        [_c_void_p] * 4 + [_c_int] * 6 + [_c_int, _c_int, _c_bool, _c_float, _c_void_p],
+    ),
     "launchLocalCorrB200PyramidBuild": (
         _c_bool,
         [_c_void_p, _c_void_p] + [_c_int] * 6 + [_c_void_p],

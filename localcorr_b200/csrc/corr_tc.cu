@@ -1513,3 +1513,87 @@ int tc_device_status(bool reset) {
 }
 
 }  // namespace lcb200
+
+// ---------------------------------------------------------------------------
+// Allocation-free forward: the tensor-core forward with its scratch in a
+// fixed device array instead of a caller workspace or an allocator, for
+// callers that may not allocate while they run (TensorRT enqueue, CUDA graph
+// capture, runtimes with memory fixed at start-up).
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_noalloc_scratch[LCB200_NOALLOC_SCRATCH_BYTES];
+
+namespace lcb200 {
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device (the host-side
+// name is only a stand-in). Looked up once per device.
+void* noalloc_scratch_ptr() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    set_error("no-alloc forward: no current CUDA device");
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      set_error(std::string("no-alloc forward: cudaGetSymbolAddress failed: ") +
+                cudaGetErrorString(e));
+      return nullptr;
+    }
+    g_noalloc_ptr[dev] = p;
+  }
+  return g_noalloc_ptr[dev];
+}
+}  // namespace
+
+}  // namespace lcb200
+
+extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
+    const void* fmap1, const void* fmap2_packed, const void* coords, void* corr, int B, int H1,
+    int W1, int C, int radius, int levels, int dtype, int coords_dtype, bool ymajor, float scale,
+    cudaStream_t stream) {
+  using namespace lcb200;
+  clear_error();
+  if (B <= 0 || (long long)H1 * W1 <= 0) return true;
+  if (levels < 1 || levels > kMaxLevels) {
+    set_error("levels must be in [1, 8] (got " + std::to_string(levels) + ")");
+    return false;
+  }
+  for (int l = 0; l < levels; ++l) {
+    if ((H1 >> l) < 1 || (W1 >> l) < 1) {
+      set_error("level " + std::to_string(l) + " of a " + std::to_string(H1) + "x" +
+                std::to_string(W1) + " map is empty");
+      return false;
+    }
+  }
+  if (coords_dtype != LCB200_F32 && coords_dtype != LCB200_F16) {
+    set_error("coords dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
+    return false;
+  }
+  std::string why;
+  if (!tc_eligible(B, H1, W1, C, radius, levels, 1, dtype, &why)) {
+    set_error("no-alloc forward supports only tensor-core configurations: " + why);
+    return false;
+  }
+  if ((reinterpret_cast<uintptr_t>(fmap1) | reinterpret_cast<uintptr_t>(fmap2_packed)) & 15) {
+    set_error("no-alloc forward: maps must be 16-byte aligned");
+    return false;
+  }
+  const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
+  if (need > LCB200_NOALLOC_SCRATCH_BYTES) {
+    set_error("no-alloc forward: this problem needs " + std::to_string(need) +
+              " bytes of scratch, more than the fixed " +
+              std::to_string((unsigned long long)LCB200_NOALLOC_SCRATCH_BYTES) +
+              " bytes the allocation-free entry point holds; use "
+              "launchLocalCorrB200PyramidForward with a workspace");
+    return false;
+  }
+  void* ws = noalloc_scratch_ptr();
+  if (!ws) return false;
+  return tc_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, C, radius, levels,
+                    coords_dtype, ymajor, scale, ws, LCB200_NOALLOC_SCRATCH_BYTES, stream);
+}

@@ -1,0 +1,91 @@
+"""The allocation-free forward entry point, checked through the C ABI.
+
+launchLocalCorrB200PyramidForwardNoAlloc exists for callers that may not
+allocate device memory while they run (a TensorRT plugin's enqueue, work
+recorded during CUDA graph capture, runtimes that reserve their memory at
+start-up). It must give the same correlation as the workspace-taking entry
+point launchLocalCorrB200PyramidForward on the tensor-core engine, call after
+call, although every call reuses the same fixed scratch array.
+
+This file is collected last on purpose; it also passes when run on its own
+in a fresh process.
+"""
+
+import math
+
+import pytest
+import torch
+
+from localcorr_b200 import _lib, ops
+from oracle import oracle
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not torch.cuda.is_available():
+        pytest.skip("CUDA device required")
+    handle = _lib.load_library()
+    assert handle is not None, "liblocalcorr_b200.so must be built"
+    return handle
+
+
+def _case(seed, b=1, c=256, h=40, w=52, levels=4):
+    f1, f2 = oracle.make_fmaps(b, c, h, w, seed=seed)
+    coords = oracle.make_coords_gauss_oob(b, h, w, 6.0, 0.05, seed=seed + 1).half().to(DEV)
+    fm1 = ops.nchw_to_nhwc(f1.half().to(DEV))
+    packed = ops.pyramid_build(f2.half().to(DEV), levels)
+    return fm1, packed, coords
+
+
+def _no_alloc(lib, fm1, packed, coords, radius, levels, scale):
+    b, h, w, c = fm1.shape
+    rd = 2 * radius + 1
+    out = torch.empty((b, levels, rd * rd, h, w), dtype=torch.float16, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+    ok = lib.launchLocalCorrB200PyramidForwardNoAlloc(
+        fm1.data_ptr(), packed.data_ptr(), coords.data_ptr(), out.data_ptr(), b, h, w, c,
+        radius, levels, _lib.F16, _lib.F16, False, scale, stream)
+    return ok, out
+
+
+def test_no_alloc_matches_workspace_forward_twice(lib):
+    lib.localCorrB200DeviceStatus(1)
+    radius, levels = 4, 4
+    scale = 1.0 / math.sqrt(256)
+    # Two calls in a row with different inputs: the shared scratch keeps the
+    # previous call's contents, which must not leak into the next result.
+    for seed in (3, 17):
+        fm1, packed, coords = _case(seed)
+        ok, out = _no_alloc(lib, fm1, packed, coords, radius, levels, scale)
+        assert ok, _lib.last_error(lib)
+        ref = ops.pyramid_corr_forward(fm1, packed, coords, radius, levels, 1, False, scale,
+                                       _lib.ENGINE_TC)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float(), ref.float(), rtol=1e-2, atol=1e-2)
+    assert lib.localCorrB200DeviceStatus(1) == 0
+
+
+def test_no_alloc_full_size_image_fits(lib):
+    # One 135x240 image of the training configuration fits the fixed scratch.
+    fm1, packed, coords = _case(5, h=135, w=240)
+    ok, out = _no_alloc(lib, fm1, packed, coords, 4, 4, 1.0 / 16)
+    assert ok, _lib.last_error(lib)
+    ref = ops.pyramid_corr_forward(fm1, packed, coords, 4, 4, 1, False, 1.0 / 16,
+                                   _lib.ENGINE_TC)
+    torch.testing.assert_close(out.float(), ref.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_no_alloc_rejects_oversize_and_unsupported(lib):
+    fm1, packed, coords = _case(7, b=4, h=135, w=240)
+    ok, _ = _no_alloc(lib, fm1, packed, coords, 4, 4, 1.0)
+    assert not ok
+    assert "bytes of scratch" in _lib.last_error(lib)
+    f32 = torch.zeros(1, 8, 8, 64, device=DEV)
+    out = torch.empty(1, 1, 81, 8, 8, device=DEV)
+    ok = lib.launchLocalCorrB200PyramidForwardNoAlloc(
+        f32.data_ptr(), f32.data_ptr(), f32.data_ptr(), out.data_ptr(), 1, 8, 8, 64, 4, 1,
+        _lib.F32, _lib.F32, False, 1.0, torch.cuda.current_stream().cuda_stream)
+    assert not ok and "tensor-core" in _lib.last_error(lib)

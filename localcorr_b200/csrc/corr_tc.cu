@@ -52,7 +52,26 @@ namespace {
 
 constexpr int kCellY = 8, kCellX = 16, kTile = 128;
 constexpr int kMaxTcLevels = 4;
-constexpr int kFwdThreads = 192;
+constexpr int kFwdThreads = 192;   // backward grad_fmap1 kernel: 6 warps
+constexpr int kBwd1Threads = 64 + 256;  // grad_fmap1: producer, MMA, 2 x 4 builder warps
+constexpr int kFwdEG = 3;          // forward epilogue warp groups
+constexpr int kFwdEpiThreads = 64 + 128 * kFwdEG;
+
+// out[i] = v[rx + i] for rx in [0, 15], without dynamic register indexing
+// (4-stage select network on the bits of rx).
+template <int NW, int NV>
+__device__ __forceinline__ void window_select(const float* v, int rx, float (&out)[NW]) {
+  static_assert(NV >= NW + 15, "window source too short");
+  float a[NW + 7], b[NW + 3], c[NW + 1];
+#pragma unroll
+  for (int i = 0; i < NW + 7; ++i) a[i] = (rx & 8) ? v[i + 8] : v[i];
+#pragma unroll
+  for (int i = 0; i < NW + 3; ++i) b[i] = (rx & 4) ? a[i + 4] : a[i];
+#pragma unroll
+  for (int i = 0; i < NW + 1; ++i) c[i] = (rx & 2) ? b[i + 2] : b[i];
+#pragma unroll
+  for (int i = 0; i < NW; ++i) out[i] = (rx & 1) ? c[i + 1] : c[i];
+}
 
 struct TcGeom {
   int B, H, W, C, r, L, RD, RD2, RDP, KC, HW;
@@ -249,7 +268,7 @@ __global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* _
 // forward
 // ---------------------------------------------------------------------------
 template <int RADIUS>
-__global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
+__global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
   constexpr int RD = 2 * RADIUS + 1;
   constexpr int NW = RD + 1;  // grid samples per window row
   extern __shared__ uint8_t smem_raw[];
@@ -261,8 +280,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_con
   const int NST = p.nstage;
   const int RDPS = g.RDP / 2 + 1;  // smem output row stride in 32-bit words (odd)
   uint32_t* sOut = reinterpret_cast<uint32_t*>(sB + (size_t)NST * p.stage_bytes);
-  float* sRow = reinterpret_cast<float*>(sOut + kTile * RDPS);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sRow + kTile * g.RS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kTile * RDPS);
   uint64_t* full = bars;
   uint64_t* empty = bars + NST;
   uint64_t* a_full = bars + 2 * NST;
@@ -279,8 +297,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_con
     for (int s = 0; s < NST; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
     tc::mbar_init(a_full, 1);
     tc::mbar_init(a_empty, 1);
-    for (int i = 0; i < 2; ++i) { tc::mbar_init(t_full + i, 1); tc::mbar_init(t_empty + i, kTile); }
-    tc::mbar_init(epi_bar, kTile);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(t_full + i, 1);
+      tc::mbar_init(t_empty + i, kTile * kFwdEG);
+    }
+    tc::mbar_init(epi_bar, kTile * kFwdEG);
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -305,17 +326,24 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_con
       const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
       if (!tc::mbar_wait(a_empty, (it & 1) ^ 1, abort)) break;
       // A tile: 128 rows x C fp16, K-major SWIZZLE_128B, 64-channel slabs.
-      const int units = g.KC * 8;
-      for (int idx = lane; idx < kTile * units; idx += 32) {
-        const int t = idx / units;
-        const int u = idx - t * units;
+      // Lane owns rows lane + 32k; its 4 pixel ids are loaded up front so the
+      // copies do not wait on dependent index loads.
+      int rid[4];
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int t = lane + 32 * k;
+        rid[k] = t < n ? p.sorted[start + t] : -1;
+      }
+      for (int u = 0; u < g.KC * 8; ++u) {
         const int kc = u >> 3, j = u & 7;
-        uint8_t* dst = sA + kc * 16384 + t * 128 + ((j ^ (t & 7)) << 4);
-        if (t < n) {
-          const int gid = p.sorted[start + t];
-          tc::cp_async_16(dst, p.fmap1 + (long long)gid * g.C + kc * 64 + j * 8, 16);
-        } else {
-          tc::cp_async_16(dst, p.fmap1, 0);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int t = lane + 32 * k;
+          uint8_t* dst = sA + kc * 16384 + t * 128 + ((j ^ (t & 7)) << 4);
+          if (rid[k] >= 0)
+            tc::cp_async_16(dst, p.fmap1 + (long long)rid[k] * g.C + kc * 64 + j * 8, 16);
+          else
+            tc::cp_async_16(dst, p.fmap1, 0);
         }
       }
       tc::cp_async_wait_all();
@@ -392,11 +420,16 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_con
     __syncwarp();
   } else {
     // ---------------- epilogue ----------------
-    const int q = warp & 3;           // TMEM lane quadrant of this warp
-    const int t = q * 32 + lane;      // tile row = pixel slot
-    const int et = threadIdx.x - 64;  // 0..127 for the cooperative copy
+    // kFwdEG groups of 4 warps; each group covers all 128 TMEM lanes (warp %
+    // 4 = lane quadrant) and takes a contiguous slice of every part's union
+    // rows, overlapping the next slice by one row (a slice's first row only
+    // seeds the bilinear pair), so the output rows are split without overlap.
+    const int q = warp & 3;               // TMEM lane quadrant of this warp
+    const int ge = (warp - 2) >> 2;       // epilogue group
+    const int t = q * 32 + lane;          // tile row = pixel slot
+    const int et = threadIdx.x - 64;      // 0..128*kFwdEG-1 for the copy
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    float* myrow = sRow + t * g.RS;
+    constexpr int NLD = (kCellX + 2 * RADIUS + 1 + 31) / 32;
     uint32_t pc = 0, ephase = 0;
     bool ok = true;
     auto epi_sync = [&]() -> bool {
@@ -426,41 +459,43 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_con
         const float clx = cx * inv, cly = cy * inv;
         const float x0f = floorf(clx), y0f = floorf(cly);
         const float dx = clx - x0f, dy = cly - y0f;
-        const float wa = (1.f - dx) * (1.f - dy), wb = dx * (1.f - dy);
-        const float wc = (1.f - dx) * dy, wd = dx * dy;
-        const int rx = (int)x0f - (cell_x0 >> l);
+        const float wa = (1.f - dx) * (1.f - dy) * p.scale, wb = dx * (1.f - dy) * p.scale;
+        const float wc = (1.f - dx) * dy * p.scale, wd = dx * dy * p.scale;
+        const int rx = (int)x0f - (cell_x0 >> l);   // 0..15
         const int ry = (int)y0f - (cell_y0 >> l);
         const int UW = g.UW[l], UH = g.UH[l], R = g.R[l];
-        float prev[NW], cur[NW];
-#pragma unroll
-        for (int k = 0; k < NW; ++k) prev[k] = 0.f;
+        __half* orow = reinterpret_cast<__half*>(sOut + t * RDPS);
         for (int k = 0; k < g.nparts[l]; ++k, ++pc) {
           const int buf = pc & 1;
           if (!tc::mbar_wait(t_full + buf, (pc >> 1) & 1, abort)) { ok = false; break; }
           tc::tc_fence_after();
           const int U0 = k * (R - 1);
-          for (int u = 0; u < R; ++u) {
-            const int U = U0 + u;
-            if (U >= UH) break;
-            for (int c = 0; c < g.nld; ++c) {
-              float v[32];
-              tc::tmem_ld32(lane_addr + buf * 256 + u * UW + 32 * c, v);
-              tc::tmem_ld_wait();
+          const int reff = min(R, UH - U0);            // rows of this part inside the union
+          const int rs = reff > 1 ? (reff - 2) / kFwdEG + 1 : 1;
+          const int ua = ge * rs;
+          const int ub = min(reff - 1, (ge + 1) * rs);
+          float prev[NW];
 #pragma unroll
-              for (int i = 0; i < 32; i += 4)
-                *reinterpret_cast<float4*>(myrow + 32 * c + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
-            }
+          for (int k2 = 0; k2 < NW; ++k2) prev[k2] = 0.f;
+          for (int u = ua; u <= ub; ++u) {
+            const int U = U0 + u;
+            float v[32 * NLD];
+#pragma unroll
+            for (int c = 0; c < NLD; ++c)
+              tc::tmem_ld32(lane_addr + buf * 256 + u * UW + 32 * c,
+                            *reinterpret_cast<float(*)[32]>(v + 32 * c));
+            tc::tmem_ld_wait();
             const int j = U - ry;  // window row of this grid row
             if (valid && j >= 0 && j <= RD) {
-#pragma unroll
-              for (int k2 = 0; k2 < NW; ++k2) cur[k2] = myrow[rx + k2];
-              if (u > 0 && j >= 1) {
+              float cur[NW];
+              window_select<NW, 32 * NLD>(v, rx, cur);
+              if (u > ua && j >= 1) {
                 const int iy = j - 1;
 #pragma unroll
                 for (int ix = 0; ix < RD; ++ix) {
                   const float val = wa * prev[ix] + wb * prev[ix + 1] + wc * cur[ix] + wd * cur[ix + 1];
                   const int d = p.ymajor ? (ix + RD * iy) : (iy + RD * ix);
-                  reinterpret_cast<__half*>(sOut + t * RDPS)[d] = __float2half_rn(val * p.scale);
+                  orow[d] = __float2half_rn(val);
                 }
               }
 #pragma unroll
@@ -475,7 +510,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_fwd_kernel(const __grid_con
         if (!epi_sync()) { ok = false; break; }
         const int words = g.RDP / 2;
         uint32_t* dst = reinterpret_cast<uint32_t*>(p.scratch + ((long long)l * g.npix + start) * g.RDP);
-        for (int i = et; i < n * words; i += kTile) {
+        for (int i = et; i < n * words; i += kTile * kFwdEG) {
           const int row = i / words;
           const int wd2 = i - row * words;
           dst[i] = sOut[row * RDPS + wd2];
@@ -592,6 +627,7 @@ struct alignas(64) TcBwdParams {
   int nstage;
   uint32_t stage_bytes;
   long long nitems;
+  int nbg;  // grad_fmap1 builder groups (1 or 2)
   TcGeom g;
 };
 
@@ -614,7 +650,7 @@ __device__ __forceinline__ void pixel_coords(const TcBwdParams& p, int b, int pi
 // union row group loaded by TMA and read as an MN-major operand (channels
 // contiguous), the same boxes the forward reads K-major.
 template <int RADIUS>
-__global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_constant__ TcBwdParams p) {
+__global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_constant__ TcBwdParams p) {
   constexpr int RD = 2 * RADIUS + 1;
   constexpr int NG = RD + 1;
   extern __shared__ uint8_t smem_raw[];
@@ -646,7 +682,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_co
       tc::mbar_init(empty + s, 1);
     }
     tc::mbar_init(acc_full, 1);
-    tc::mbar_init(acc_empty, kTile);
+    tc::mbar_init(acc_empty, p.nbg * kTile);
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -729,7 +765,11 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_co
     __syncwarp();
   } else {
     // ---------------- builders + epilogue ----------------
+    // Two groups of 4 warps (each group covers the 128 TMEM lanes): group gb
+    // builds the A tiles of the stages with (stage index & 1) == gb, and
+    // reads columns [gb*C/2, (gb+1)*C/2) of the accumulator at chunk end.
     const int q = warp & 3;
+    const int gb = (warp - 2) >> 2;
     const int t = q * 32 + lane;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t gs = 0;
@@ -755,7 +795,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_co
         const int UW = g.UW[l], Rg = g.Rg[l];
         // This pixel's gint row -> per-thread shared scratch (global loads
         // batched ahead of the shared stores).
-        __half* grow = reinterpret_cast<__half*>(smem + (size_t)NST * SB + 256) + (size_t)t * g.RDQ;
+        __half* grow = reinterpret_cast<__half*>(smem + (size_t)NST * SB + 256) +
+                       (size_t)(gb * kTile + t) * g.RDQ;
         if (valid) {
           const uint4* src = reinterpret_cast<const uint4*>(p.gint + ((long long)l * g.npix + idx) * g.RDQ);
           uint4 tmp[(NG * NG + 7) / 8];
@@ -765,12 +806,14 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_co
           for (int i = 0; i < (NG * NG + 7) / 8; ++i) reinterpret_cast<uint4*>(grow)[i] = tmp[i];
         }
         for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
+          if ((int)(gs % (uint32_t)p.nbg) != gb) continue;
           const int s = gs % NST;
           const uint32_t use = gs / NST;
           if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
           uint8_t* arow = smem + (size_t)s * SB + t * 128;
 #pragma unroll
-          for (int j = 0; j < 8; ++j) reinterpret_cast<uint4*>(arow)[j] = make_uint4(0, 0, 0, 0);
+          for (int j = 0; j < 8; ++j)
+            reinterpret_cast<uint4*>(arow)[j ^ (t & 7)] = make_uint4(0, 0, 0, 0);
           if (valid) {
             const int u0 = max(gi * Rg, ry), u1 = min(gi * Rg + Rg - 1, ry + RD);
             for (int U = u0; U <= u1; ++U) {
@@ -792,7 +835,7 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_co
       // epilogue: TMEM row t = this pixel's grad_fmap1 (fp32) -> fp16 row
       if (!tc::mbar_wait(acc_full, it & 1, abort)) { ok = false; break; }
       tc::tc_fence_after();
-      for (int c0 = 0; c0 < g.C; c0 += 32) {
+      for (int c0 = gb * (g.C / p.nbg); c0 < (gb + 1) * (g.C / p.nbg); c0 += 32) {
         float v[32];
         tc::tmem_ld32(lane_addr + c0, v);
         tc::tmem_ld_wait();
@@ -830,7 +873,8 @@ __global__ void __launch_bounds__(kFwdThreads, 1) tc_bwd1_kernel(const __grid_co
 // B (MN-major: the fmap1 row, cp.async). D is double-buffered in TMEM; the
 // epilogue adds it to the float32 gradient with red.global.add.v4.f32 (an
 // item may cover only part of Q's cells, so items of one Q add up).
-constexpr int kBwd2Threads = 288;  // warp 0 MMA, 1-4 builders, 5-8 epilogue
+constexpr int kBwd2Builders = 256;  // builder threads (warps 1..8)
+constexpr int kBwd2Threads = 32 + kBwd2Builders + 128;  // + MMA warp 0, 4 epilogue warps
 
 struct Bwd2Item {
   int l, b, qy0, qx0, ra, rb, ca, cb;  // level, batch, tile origin, cell rows/cols
@@ -902,7 +946,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       tc::mbar_init(empty + s, 1);
     }
     for (int i = 0; i < 2; ++i) { tc::mbar_init(acc_full + i, 1); tc::mbar_init(acc_empty + i, kTile); }
-    tc::mbar_init(bsync_bar, kTile);
+    tc::mbar_init(bsync_bar, kBwd2Builders);
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -934,6 +978,9 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           const int s = gs % NST;
           const uint32_t use = gs / NST;
           if (!tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
+          // Rows arrive through cp.async completion: make their shared-memory
+          // writes visible to the tensor core's (async) proxy.
+          tc::fence_proxy_async_smem();
           tc::tc_fence_after();
           const int flags = stage_flags[s];
           stage_flags[s] = 0;
@@ -957,16 +1004,18 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       tc::mbar_wait(fin_bar, 0, abort);
     }
     __syncwarp();
-  } else if (warp <= 4) {
+  } else if (warp <= kBwd2Builders / 32) {
     // ---------------- builders ----------------
     // Kept (pixel, Q) pairs get consecutive rows of the item through one
     // shared counter; row r of the item goes to stage item_first + r/128.
-    // Each row writer arrives once on its stage's afull barrier; at the end
-    // of the item the rows of the closing stage past the last kept pixel
-    // are zeroed and arrive too, so every stage sees exactly 128 arrivals.
-    const int bw = warp - 1;          // builder warp 0..3
-    const int bt = bw * 32 + lane;    // builder thread 0..127
-    uint8_t* scr = smem + (size_t)NST * SB + 512 + (size_t)bt * g.RDQ * 2;
+    // Each row's A part (its G restricted to Q) is written with plain
+    // stores from registers, its B part (the fmap1 row) by cp.async whose
+    // completion arrives on the stage's afull barrier by itself
+    // (cp.async.mbarrier.arrive.noinc), so no builder waits on its copies.
+    // At the end of an item the closing stage's unused rows are zeroed and
+    // arrive too: every stage sees exactly 128 arrivals.
+    constexpr int NGW = (NG * NG + 7) / 8;  // uint4 words of a gint row
+    const int bt = threadIdx.x - 32;         // builder thread 0..kBwd2Builders-1
     uint32_t gs0 = 0, bphase = 0;
     bool ok = true;
     auto bsync = [&]() -> bool {
@@ -986,12 +1035,13 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         const long long c1 = (long long)item.b * g.ncell + (long long)cyr * g.ncx + item.cb;
         const int s0 = p.offsets[c0];
         const int s1 = p.offsets[c1] + p.counts[c1];
-        for (int base = s0; base < s1; base += kTile) {
+        for (int base = s0; base < s1; base += kBwd2Builders) {
           const int pos = base + bt;
           bool touch = false;
-          int x0 = 0, y0 = 0, ylo = 0, yhi = -1, xlo = 0, xhi = -1;
+          int x0 = 0, y0 = 0, ylo = 0, yhi = -1, xlo = 0, xhi = -1, gid = 0;
           if (pos < s1) {
             const int pk = sb_l[pos];
+            gid = p.sorted[pos];
             x0 = (int)(short)(pk & 0xFFFF);
             y0 = pk >> 16;
             ylo = max(max(y0 - RADIUS, item.qy0), 0);
@@ -1006,17 +1056,12 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           if (lane == 0) first = atomicAdd(&item_rows, __popc(ballot));
           first = __shfl_sync(0xffffffffu, first, 0);
           if (!touch) continue;
-          // gint row of this pixel -> per-thread scratch (global loads
-          // batched ahead of the shared stores)
-          const uint4* grow = reinterpret_cast<const uint4*>(
-              p.gint + ((long long)l * g.npix + pos) * g.RDQ);
-          const int gid = p.sorted[pos];
+          uint4 gr[NGW];
           {
-            uint4 tmp[(NG * NG + 7) / 8];
+            const uint4* src = reinterpret_cast<const uint4*>(
+                p.gint + ((long long)l * g.npix + pos) * g.RDQ);
 #pragma unroll
-            for (int i = 0; i < (NG * NG + 7) / 8; ++i) tmp[i] = grow[i];
-#pragma unroll
-            for (int i = 0; i < (NG * NG + 7) / 8; ++i) reinterpret_cast<uint4*>(scr)[i] = tmp[i];
+            for (int i = 0; i < NGW; ++i) gr[i] = src[i];
           }
           const int r = first + __popc(ballot & lt_mask);
           const uint32_t st = gs0 + (uint32_t)(r / kTile);
@@ -1025,32 +1070,65 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           if (!tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort)) { ok = false; continue; }
           uint8_t* A = smem + (size_t)s * SB;
           uint8_t* Bm = A + 32768;
+          // (16-byte units are XOR-swizzled by row & 7 everywhere a thread
+          // owns a 128-byte row: rows of a warp then hit distinct banks.)
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int j = 0; j < 8; ++j)
+              *reinterpret_cast<uint4*>(A + m * 16384 + row * 128 + ((j ^ (row & 7)) << 4)) =
+                  make_uint4(0, 0, 0, 0);
+          // G restricted to Q. The gint row is parked in this row's own B
+          // bytes (not loaded yet) so the intersection loop can index it;
+          // the fmap1 cp.async below overwrites it after the last read.
+          if (NGW * 16 <= g.KC * 128) {
+#pragma unroll
+            for (int i = 0; i < NGW; ++i)
+              *reinterpret_cast<uint4*>(Bm + (i >> 3) * 16384 + row * 128 + (((i & 7) ^ (row & 7)) << 4)) = gr[i];
+            for (int yy = ylo; yy <= yhi; ++yy) {
+              const int e0 = (yy - (y0 - RADIUS)) * NG - (x0 - RADIUS);
+              const int p0 = (yy - item.qy0) * 16 - item.qx0;
+              for (int xx = xlo; xx <= xhi; ++xx) {
+                const int e = e0 + xx;
+                const unsigned short hb = *reinterpret_cast<const unsigned short*>(
+                    Bm + (e >> 6) * 16384 + row * 128 + (((((e & 63) >> 3) ^ (row & 7))) << 4) +
+                    (e & 7) * 2);
+                const int pq = p0 + xx;
+                const int m = pq >> 6, cc = pq & 63;
+                *reinterpret_cast<unsigned short*>(A + m * 16384 + row * 128 +
+                                                   ((((cc >> 3) ^ (row & 7))) << 4) + (cc & 7) * 2) = hb;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int jj = 0; jj < NG; ++jj) {
+              const int yy = y0 - RADIUS + jj;
+              const bool rin = yy >= ylo && yy <= yhi;
+#pragma unroll
+              for (int kk = 0; kk < NG; ++kk) {
+                const int xx = x0 - RADIUS + kk;
+                if (rin && xx >= xlo && xx <= xhi) {
+                  const int e = jj * NG + kk;
+                  const uint4 q4 = gr[e >> 3];
+                  const int wsel = (e & 7) >> 1;
+                  const uint32_t wv = wsel == 0 ? q4.x : wsel == 1 ? q4.y : wsel == 2 ? q4.z : q4.w;
+                  const unsigned short hb = (e & 1) ? (unsigned short)(wv >> 16) : (unsigned short)(wv & 0xFFFF);
+                  const int pq = (yy - item.qy0) * 16 + (xx - item.qx0);
+                  const int m = pq >> 6, cc = pq & 63;
+                  *reinterpret_cast<unsigned short*>(A + m * 16384 + row * 128 +
+                                                     ((((cc >> 3) ^ (row & 7))) << 4) + (cc & 7) * 2) = hb;
+                }
+              }
+            }
+          }
+          tc::fence_proxy_async_smem();
           const __half* f1 = p.fmap1 + (long long)gid * g.C;
           for (int kc = 0; kc < g.KC; ++kc)
 #pragma unroll
             for (int j = 0; j < 8; ++j)
               tc::cp_async_16(Bm + kc * 16384 + row * 128 + ((j ^ (row & 7)) << 4),
                               f1 + kc * 64 + j * 8, 16);
-#pragma unroll
-          for (int m = 0; m < 2; ++m)
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              *reinterpret_cast<uint4*>(A + m * 16384 + row * 128 + (j << 4)) = make_uint4(0, 0, 0, 0);
-          const __half* gsm = reinterpret_cast<const __half*>(scr);
-          for (int yy = ylo; yy <= yhi; ++yy) {
-            const int jrow = (yy - (y0 - RADIUS)) * NG - (x0 - RADIUS);
-            const int prow = (yy - item.qy0) * 16 - item.qx0;
-            for (int xx = xlo; xx <= xhi; ++xx) {
-              const int pq = prow + xx;
-              const int m = pq >> 6, cc = pq & 63;
-              *reinterpret_cast<__half*>(A + m * 16384 + row * 128 +
-                                         ((((cc >> 3) ^ (row & 7))) << 4) + (cc & 7) * 2) =
-                  gsm[jrow + xx];
-            }
-          }
-          tc::cp_async_wait_all();
-          tc::fence_proxy_async_smem();
-          tc::mbar_arrive(afull + s);
+          tc::cp_async_mbar_arrive_noinc(afull + s);
         }
       }
       if (!ok) break;
@@ -1065,19 +1143,22 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         else stage_flags[s] = 1 | (T > 0 ? 2 : 0);
       }
       if (!bsync() || !ok) { ok = false; break; }
-      if (bt >= fill) {
+      if (bt < kTile && bt >= fill) {
         if (!tc::mbar_wait(empty + s, ((cs / NST) & 1) ^ 1, abort)) { ok = false; break; }
         uint8_t* A = smem + (size_t)s * SB;
 #pragma unroll
         for (int m = 0; m < 2; ++m)
 #pragma unroll
           for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<uint4*>(A + m * 16384 + bt * 128 + (j << 4)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(A + m * 16384 + bt * 128 + ((j ^ (bt & 7)) << 4)) =
+                make_uint4(0, 0, 0, 0);
         tc::fence_proxy_async_smem();
         tc::mbar_arrive(afull + s);
       }
       gs0 = cs + 1;
     }
+    // Copies still in flight complete before the kernel's final barrier.
+    tc::cp_async_wait_all();
   } else {
     // ---------------- epilogue ----------------
     const int q = warp & 3;
@@ -1246,8 +1327,7 @@ size_t fwd_smem_bytes(const TcGeom& g, int nstage, uint32_t* stage_bytes) {
   if (stage_bytes) *stage_bytes = sb;
   const size_t rdps = g.RDP / 2 + 1;
   const size_t need = 1024 /*alignment slack*/ + (size_t)g.KC * 16384 + (size_t)nstage * sb +
-                      (size_t)kTile * rdps * 4 + (size_t)kTile * g.RS * 4 + (2 * nstage + 8) * 8 +
-                      16;
+                      (size_t)kTile * rdps * 4 + (2 * nstage + 8) * 8 + 16;
   // At least half of the SM's shared memory: one CTA per SM, so the
   // 512-column TMEM allocation never waits on a co-resident CTA.
   return std::max<size_t>(need, 120 * 1024);
@@ -1279,7 +1359,7 @@ template <int RADIUS>
 bool launch_fwd_kernel(const TcFwdParams& prm, size_t smem, cudaStream_t s) {
   auto k = tc_fwd_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k, smem)) return false;
-  k<<<num_sms(), kFwdThreads, smem, s>>>(prm);
+  k<<<num_sms(), kFwdEpiThreads, smem, s>>>(prm);
   count_launch();
   return check_launch("tc_fwd");
 }
@@ -1388,14 +1468,19 @@ bool bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dila
   int nf = 0;
   if (!eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, &g, &nf)) return false;
   if (g.RDQ == 0) return false;
-  const int n1 = pick_stages(bwd1_stage_bytes(g), 256 + (size_t)kTile * g.RDQ * 2, 4);
-  const int n2 = pick_stages(bwd2_stage_bytes(g), 512 + (size_t)kTile * g.RDQ * 2, 2);
+  int nbg = 2;
+  int n1 = pick_stages(bwd1_stage_bytes(g), 256 + (size_t)2 * kTile * g.RDQ * 2, 4);
+  if (n1 < 3) {
+    nbg = 1;
+    n1 = pick_stages(bwd1_stage_bytes(g), 256 + (size_t)kTile * g.RDQ * 2, 4);
+  }
+  const int n2 = pick_stages(bwd2_stage_bytes(g), 512, 2);
   if (n1 < 2 || n2 < 2) {
     if (why) *why = "tensor-core backward shared-memory budget exceeded";
     return false;
   }
   if (out) *out = g;
-  if (nst1) *nst1 = n1;
+  if (nst1) *nst1 = n1 * 4 + nbg;  // packed: stages, builder groups
   if (nst2) *nst2 = n2;
   return true;
 }
@@ -1410,14 +1495,14 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
                                             ymajor, g);
   count_launch();
   if (!check_launch("tc_gint")) return false;
-  const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256 + (size_t)kTile * g.RDQ * 2;
+  const size_t smem1 =
+      1024 + (size_t)p1.nstage * p1.stage_bytes + 256 + (size_t)p1.nbg * kTile * g.RDQ * 2;
   auto k1 = tc_bwd1_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k1, smem1)) return false;
-  k1<<<num_sms(), kFwdThreads, smem1, s>>>(p1);
+  k1<<<num_sms(), 64 + 128 * p1.nbg, smem1, s>>>(p1);
   count_launch();
   if (!check_launch("tc_bwd1")) return false;
-  const size_t smem2 = std::max<size_t>(
-      1024 + (size_t)p2.nstage * p2.stage_bytes + 512 + (size_t)kTile * g.RDQ * 2, 120 * 1024);
+  const size_t smem2 = std::max<size_t>(1024 + (size_t)p2.nstage * p2.stage_bytes + 512, 120 * 1024);
   auto k2 = tc_bwd2_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k2, smem2)) return false;
   k2<<<num_sms(), kBwd2Threads, smem2, s>>>(p2);
@@ -1489,7 +1574,9 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.g = g;
   p1.nitems = g.items_before[levels];
   TcBwdParams p2 = p1;
-  p1.nstage = n1;
+  p1.nstage = n1 / 4;
+  p1.nbg = n1 % 4;
+  p2.nbg = 1;
   p1.stage_bytes = (uint32_t)bwd1_stage_bytes(g);
   p2.nstage = n2;
   p2.stage_bytes = (uint32_t)bwd2_stage_bytes(g);

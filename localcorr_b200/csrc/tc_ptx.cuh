@@ -86,6 +86,12 @@ __device__ __forceinline__ void cp_async_16(void* dst, const void* src, uint32_t
                "r"(src_bytes)
                : "memory");
 }
+// Arrive on `bar` once every cp.async this thread issued so far has
+// landed; the arrival counts toward the barrier's expected count.
+__device__ __forceinline__ void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
 __device__ __forceinline__ void cp_async_wait_all() {
   asm volatile("cp.async.wait_all;" ::: "memory");
 }

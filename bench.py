@@ -104,6 +104,7 @@ class ClockSampler:
         self.gpu = gpu_index
         self.proc = None
         self.lines = []
+        self.mark = 0
         self._thr = None
 
     def start(self):
@@ -117,6 +118,12 @@ class ClockSampler:
             return
         self._thr = threading.Thread(target=self._read, daemon=True)
         self._thr.start()
+        # nvidia-smi needs about a second to print its first sample; the timed
+        # region starts only once sampling runs, and earlier samples are dropped.
+        t0 = time.time()
+        while not self.lines and time.time() - t0 < 10.0 and self.proc.poll() is None:
+            time.sleep(0.05)
+        self.mark = len(self.lines)
 
     def _read(self):
         for line in self.proc.stdout:
@@ -134,7 +141,8 @@ class ClockSampler:
             self._thr.join(timeout=2)
         sm, smax, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        lines = self.lines[self.mark:] or self.lines
+        for ln in lines:
             parts = [x.strip() for x in ln.split(",")]
             if len(parts) < 9:
                 continue
@@ -277,7 +285,7 @@ def reference_arm(args, cfg, cfg_name):
 def main(argv=None):
     ap = argparse.ArgumentParser(description=__doc__)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=60)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=DEFAULT, choices=sorted(CONFIGS))

@@ -16,7 +16,7 @@ bool simt_backward(const void*, const void*, const void*, const void*, void*, fl
                    int, int, int, int, int, int, int, int, bool, float, cudaStream_t);
 bool tc_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
                  int dtype, std::string* why);
-size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels);
+size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels, bool backward);
 bool tc_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
                 int, bool, float, void*, size_t, cudaStream_t);
 bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int, int,
@@ -202,7 +202,7 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
   }
   bool ok = true;
   if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok, false, f1, f2)) {
-    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
+    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels, false);
     if (lib_ws) {
       ws = library_scratch(need, s);
       ws_bytes = ws ? need : 0;
@@ -240,7 +240,7 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
   }
   bool ok = true;
   if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok, true, f1, f2)) {
-    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
+    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels, true);
     if (lib_ws) {
       ws = library_scratch(need, s);
       ws_bytes = ws ? need : 0;
@@ -309,7 +309,7 @@ size_t localCorrB200PyramidWorkspaceBytes(int B, int H1, int W1, int C, int radi
   ok = true;
   const bool b = use_tc(engine, B, H1, W1, C, radius, levels, dilation, dtype, &ok, true);
   if (!f && !b) return 0;
-  return tc_workspace_bytes(B, H1, W1, C, radius, levels);
+  return tc_workspace_bytes(B, H1, W1, C, radius, levels, b);
 }
 
 bool launchLocalCorrB200PyramidForward(const void* fmap1, const void* fmap2_packed,

@@ -32,7 +32,8 @@
 // Warp roles of the forward kernel (persistent, one CTA per SM):
 //   warp 0      producer: cp.async gather of the A tile, TMA loads of B boxes
 //   warp 1      TMEM owner and MMA issuer (one thread)
-//   warps 2..5  epilogue (TMEM lane quadrant = warp % 4)
+//   warps 2..13 epilogue: three groups of four warps (TMEM lane quadrant =
+//               warp % 4) that share out the rows of each part
 // Every mbarrier wait is bounded (2 s); on timeout the kernel records an
 // error status, all roles wind down, TMEM is freed and the kernel returns.
 #include <cub/block/block_scan.cuh>
@@ -52,7 +53,6 @@ namespace {
 
 constexpr int kCellY = 8, kCellX = 16, kTile = 128;
 constexpr int kMaxTcLevels = 4;
-constexpr int kFwdThreads = 192;   // backward grad_fmap1 kernel: 6 warps
 constexpr int kBwd1Threads = 64 + 256;  // grad_fmap1: producer, MMA, 2 x 4 builder warps
 constexpr int kFwdEG = 3;          // forward epilogue warp groups
 constexpr int kFwdEpiThreads = 64 + 128 * kFwdEG;
@@ -86,7 +86,9 @@ struct TcGeom {
   // backward: integer-grid weights per pixel/level ((RD+1)^2, padded), the
   // union row groups of <= 64 positions (grad_fmap1 K chunks), and the
   // output-tile work decomposition of grad_fmap2
-  int NG, RDQ;
+  int NG;
+  int NU;  // 16-byte units of one pre-shifted grid row (grad_fmap2 records)
+  int UWb[kMaxTcLevels];  // grad_fmap1 box width: 8-aligned origin, multiple of 8
   int Rg[kMaxTcLevels], ngroups[kMaxTcLevels];
   int nqy[kMaxTcLevels], nqx[kMaxTcLevels], rpi[kMaxTcLevels], qgroups[kMaxTcLevels];
   long long items_before[kMaxTcLevels + 1];  // grad_fmap2 items, coarse levels first
@@ -144,13 +146,22 @@ bool make_tc_geom(int B, int H, int W, int C, int r, int L, TcGeom* g, std::stri
     t.maxN = std::max(t.maxN, t.npad[l]);
   }
   t.NG = t.RD + 1;
-  t.RDQ = round_up(t.NG * t.NG, 8);
+  t.NU = ceil_div(t.NG + 7, 8);
   for (int l = 0; l < L; ++l) {
-    if (t.UW[l] > 64) {
+    // grad_fmap1 boxes start at the 8-aligned column at or left of the union
+    // origin (cell_x0 >> l) - r, so that record units (8-aligned positions)
+    // land on whole 16-byte units of the box rows.
+    int shift = 0;
+    for (int m = 0; m < 8; ++m) {
+      const int x0 = ((t.xlo + m * kCellX) >> l) - r;
+      shift = std::max(shift, x0 - (x0 & ~7));
+    }
+    t.UWb[l] = round_up(t.UW[l] + shift, 8);
+    if (t.UWb[l] > 64) {
       if (why) *why = "union rows wider than 64 positions";
       return false;
     }
-    t.Rg[l] = 64 / t.UW[l];
+    t.Rg[l] = 64 / t.UWb[l];
     t.ngroups[l] = ceil_div(t.UH[l], t.Rg[l]);
     // grad_fmap2 tiles of 8x16 level-l positions; a tile pulls the pixels of
     // the anchor cells whose level-l windows can reach it, split into items
@@ -541,72 +552,156 @@ __global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_
 // which are the reference backward's per-tap sums
 // (cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:887-916) regrouped.
 
-// Source-order pass: reads corr_grad (coalesced along W), writes the pixel's
-// G rows in sorted order gint[l][idx][RDQ] (fp16), and zeroes grad_fmap1 of
-// pixels dropped by the sort (windows off the map at every level).
+// Source-order pass over 128-pixel runs of one (batch, level): the run's
+// incoming gradients (RD^2 rows of 128 pixels) are staged in shared memory
+// with 16-byte loads, each thread collapses its pixel's onto the (RD+1)^2
+// grid one grid row at a time (separable weights: a horizontal lerp of two
+// tap rows, then a vertical one), and writes the pixel's record
+//   gsh[l][idx][NG][NU] (16-byte units, sorted order): grid row j shifted
+//   right by a = (x0 - r) mod 8 halves inside NU*8 zero-padded halves,
+// so a record unit covers the 8 positions [X + 8u, X + 8u + 8) with
+// X = (x0 - r) - a, a multiple of 8; grad_fmap2 and grad_fmap1 builders
+// copy these units into 8-aligned position units with cp.async as they are.
+// Records go out through a per-warp shared staging area, RC grid rows at a
+// time, as contiguous runs. It also records the packed level bases and
+// zeroes grad_fmap1 of pixels dropped by the sort (windows off the map at
+// every level).
+template <int RADIUS>
+struct GintShape {
+  static constexpr int RD = 2 * RADIUS + 1;
+  static constexpr int NG = RD + 1;
+  static constexpr int NU = (NG + 14) / 8;                 // units per shifted row
+  static constexpr int RC = (16 / NU) < NG ? 16 / NU : NG;  // grid rows per staged chunk
+  static constexpr int SU = (RC * NU) % 2 ? RC * NU : RC * NU + 1;  // odd unit stride
+  static constexpr size_t tile_bytes = (size_t)RD * RD * 128 * 2;
+  static constexpr size_t smem_bytes = tile_bytes + (size_t)4 * 32 * SU * 16;
+};
+
 template <int RADIUS>
 __global__ void __launch_bounds__(128)
 tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
-               int coords_f32, const int* __restrict__ inv, __half* __restrict__ gint,
+               int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
                int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale, int ymajor,
-               TcGeom g) {
-  constexpr int RD = 2 * RADIUS + 1;
-  constexpr int NG = RD + 1;
-  const int pix = blockIdx.x * blockDim.x + threadIdx.x;
+               int vec_ok, TcGeom g) {
+  using S = GintShape<RADIUS>;
+  constexpr int RD = S::RD, NG = S::NG, NU = S::NU, RC = S::RC, SU = S::SU;
+  constexpr unsigned FULL = 0xffffffffu;
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __half* tile = reinterpret_cast<__half*>(gsm);
+  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
+  uint4* stage = reinterpret_cast<uint4*>(gsm + S::tile_bytes) + warp * 32 * SU;
+  const int pix0 = blockIdx.x * 128;
   const int l = blockIdx.y;
   const int b = blockIdx.z;
-  if (pix >= g.HW) return;
-  const long long gid = (long long)b * g.HW + pix;
-  const int idx = inv[gid];
-  if (idx < 0) {
-    if (l == 0) {
-      uint4* row = reinterpret_cast<uint4*>(grad_f1 + gid * g.C);
-      for (int i = 0; i < g.C / 8; ++i) row[i] = make_uint4(0, 0, 0, 0);
+  const int npx = min(128, g.HW - pix0);
+  const __half* src = corr_grad + ((long long)b * g.L + l) * RD * RD * g.HW + pix0;
+  if (vec_ok && npx == 128) {
+#pragma unroll 4
+    for (int i = t; i < RD * RD * 16; i += 128) {
+      const int d = i >> 4, c = i & 15;
+      reinterpret_cast<uint4*>(tile)[i] =
+          *reinterpret_cast<const uint4*>(src + (long long)d * g.HW + c * 8);
     }
-    return;
-  }
-  float cx, cy;
-  if (coords_f32) {
-    const float* co = reinterpret_cast<const float*>(coords) + (long long)b * 2 * g.HW + pix;
-    cx = co[0]; cy = co[g.HW];
   } else {
-    const __half* co = reinterpret_cast<const __half*>(coords) + (long long)b * 2 * g.HW + pix;
-    cx = __half2float(co[0]); cy = __half2float(co[g.HW]);
-  }
-  const float inv_s = 1.f / (float)(1 << l);
-  const float clx = cx * inv_s, cly = cy * inv_s;
-  const float dx = clx - floorf(clx), dy = cly - floorf(cly);
-  // Level-l integer base of the window, packed (x low, y high, int16 each),
-  // in sorted order: the grad_fmap2 pull reads it coalesced per candidate.
-  sbase[(long long)l * g.npix + idx] =
-      ((int)floorf(clx) & 0xFFFF) | ((int)floorf(cly) << 16);
-  const float wa = (1.f - dx) * (1.f - dy) * scale, wb = dx * (1.f - dy) * scale;
-  const float wc = (1.f - dx) * dy * scale, wd = dx * dy * scale;
-  const __half* src = corr_grad + ((long long)b * g.L + l) * RD * RD * g.HW + pix;
-  float gr[RD * RD];
-#pragma unroll
-  for (int d = 0; d < RD * RD; ++d) gr[d] = __half2float(src[(long long)d * g.HW]);
-  auto gv = [&](int iy, int ix) -> float {
-    return gr[ymajor ? (ix + RD * iy) : (iy + RD * ix)];
-  };
-  uint4* dst = reinterpret_cast<uint4*>(gint + ((long long)l * g.npix + idx) * g.RDQ);
-#pragma unroll
-  for (int e0 = 0; e0 < NG * NG; e0 += 8) {
-    __align__(16) __half hv[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) {
-      const int ee = e0 + e;
-      float v = 0.f;
-      if (ee < NG * NG) {
-        const int j = ee / NG, k = ee % NG;
-        if (j < RD && k < RD) v += gv(j, k) * wa;
-        if (j < RD && k >= 1) v += gv(j, k - 1) * wb;
-        if (j >= 1 && k < RD) v += gv(j - 1, k) * wc;
-        if (j >= 1 && k >= 1) v += gv(j - 1, k - 1) * wd;
-      }
-      hv[e] = __float2half_rn(v);
+    for (int i = t; i < RD * RD * 128; i += 128) {
+      const int d = i >> 7, c = i & 127;
+      tile[i] = c < npx ? src[(long long)d * g.HW + c] : __float2half(0.f);
     }
-    dst[e0 / 8] = *reinterpret_cast<const uint4*>(hv);
+  }
+  const int pix = pix0 + t;
+  int idx = -1;
+  float dx = 0.f, dy = 0.f;
+  int x0 = 0;
+  if (pix < g.HW) {
+    const long long gid = (long long)b * g.HW + pix;
+    idx = inv[gid];
+    if (idx < 0) {
+      if (l == 0) {
+        uint4* row = reinterpret_cast<uint4*>(grad_f1 + gid * g.C);
+        for (int i = 0; i < g.C / 8; ++i) row[i] = make_uint4(0, 0, 0, 0);
+      }
+    } else {
+      float cx, cy;
+      if (coords_f32) {
+        const float* co = reinterpret_cast<const float*>(coords) + (long long)b * 2 * g.HW + pix;
+        cx = co[0]; cy = co[g.HW];
+      } else {
+        const __half* co = reinterpret_cast<const __half*>(coords) + (long long)b * 2 * g.HW + pix;
+        cx = __half2float(co[0]); cy = __half2float(co[g.HW]);
+      }
+      const float inv_s = 1.f / (float)(1 << l);
+      const float clx = cx * inv_s, cly = cy * inv_s;
+      dx = clx - floorf(clx);
+      dy = cly - floorf(cly);
+      x0 = (int)floorf(clx);
+      const int y0 = (int)floorf(cly);
+      // Level-l integer base of the window, packed (x low, y high, int16
+      // each), in sorted order: the grad_fmap2 pull reads it per candidate.
+      sbase[(long long)l * g.npix + idx] = (x0 & 0xFFFF) | (y0 << 16);
+    }
+  }
+  __syncthreads();
+  // Shift by a halves: one byte permute (odd part) and two word selects.
+  const int a = (x0 - RADIUS) & 7;
+  const uint32_t sel = (a & 1) ? 0x5432u : 0x7654u;
+  const bool s1 = (a & 2) != 0, s2 = (a & 4) != 0;
+  const float ex = 1.f - dx, ey = (1.f - dy) * scale, fy = dy * scale;
+  auto tap = [&](int iy, int ix) -> float {
+    return __half2float(tile[(ymajor ? (ix + RD * iy) : (iy + RD * ix)) * 128 + t]);
+  };
+  float hp[NG];
+#pragma unroll
+  for (int k = 0; k < NG; ++k) hp[k] = 0.f;
+#pragma unroll
+  for (int j0 = 0; j0 < NG; j0 += RC) {
+#pragma unroll
+    for (int j = j0; j < j0 + RC && j < NG; ++j) {
+      float hc[NG];
+      if (j < RD) {
+        float tr[RD];
+#pragma unroll
+        for (int k = 0; k < RD; ++k) tr[k] = tap(j, k);
+#pragma unroll
+        for (int k = 0; k < NG; ++k)
+          hc[k] = (k < RD ? ex * tr[k] : 0.f) + (k >= 1 ? dx * tr[k - 1] : 0.f);
+      } else {
+#pragma unroll
+        for (int k = 0; k < NG; ++k) hc[k] = 0.f;
+      }
+      uint32_t q[4 * NU];
+#pragma unroll
+      for (int k = 0; k < 4 * NU; ++k) {
+        uint32_t w[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int c = 2 * k + h;
+          w[h] = c < NG ? (uint32_t)__half_as_ushort(__float2half_rn(ey * hc[c] + fy * hp[c])) : 0u;
+        }
+        q[k] = w[0] | (w[1] << 16);
+      }
+#pragma unroll
+      for (int k = 4 * NU - 1; k >= 0; --k) q[k] = __byte_perm(k >= 1 ? q[k - 1] : 0u, q[k], sel);
+#pragma unroll
+      for (int k = 4 * NU - 1; k >= 0; --k) q[k] = s1 ? (k >= 1 ? q[k - 1] : 0u) : q[k];
+#pragma unroll
+      for (int k = 4 * NU - 1; k >= 0; --k) q[k] = s2 ? (k >= 2 ? q[k - 2] : 0u) : q[k];
+#pragma unroll
+      for (int u = 0; u < NU; ++u)
+        stage[lane * SU + (j - j0) * NU + u] = make_uint4(q[4 * u], q[4 * u + 1], q[4 * u + 2], q[4 * u + 3]);
+#pragma unroll
+      for (int k = 0; k < NG; ++k) hp[k] = hc[k];
+    }
+    __syncwarp();
+    // the warp's 32 records, rows [j0, j0 + RC): contiguous runs per pixel
+    constexpr int CU0 = RC * NU;
+    const int CU = (j0 + RC <= NG ? RC : NG - j0) * NU;
+    for (int f = lane; f < 32 * CU0; f += 32) {
+      const int k = f / CU0, v = f - k * CU0;
+      const int idk = __shfl_sync(FULL, idx, k);
+      if (idk >= 0 && v < CU)
+        gsh[((long long)l * g.npix + idk) * (NG * NU) + j0 * NU + v] = stage[k * SU + v];
+    }
+    __syncwarp();
   }
 }
 
@@ -618,7 +713,7 @@ struct alignas(64) TcBwdParams {
   const int* offsets;
   const int4* work;
   const int* work_count;
-  const __half* gint;
+  const uint4* gsh;
   const int* sbase;
   const __half* fmap1;
   __half* grad_f1;
@@ -646,13 +741,16 @@ __device__ __forceinline__ void pixel_coords(const TcBwdParams& p, int b, int pi
 // grad_fmap1, per 128-pixel chunk: D[128 px x C] += G[128 px x 64 pos] *
 // F2[64 pos x C] over every union row group of every level; D lives in TMEM
 // for the whole chunk, so each pixel row is written once (no atomics).
-// A (G rows) is built by the builder warps (K-major, SWIZZLE_128B); B is the
-// union row group loaded by TMA and read as an MN-major operand (channels
-// contiguous), the same boxes the forward reads K-major.
+// A (G rows, K-major, SWIZZLE_128B) is built by the builder warps from the
+// pixel's pre-shifted grid records: the group's boxes start at an 8-aligned
+// column and have a width that is a multiple of 8, so every 16-byte A unit is
+// one record unit (cp.async) or zeros. B is the union row group loaded by
+// TMA and read as an MN-major operand (channels contiguous).
 template <int RADIUS>
 __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_constant__ TcBwdParams p) {
   constexpr int RD = 2 * RADIUS + 1;
   constexpr int NG = RD + 1;
+  constexpr int NU = (NG + 14) / 8;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
   const TcGeom& g = p.g;
@@ -709,9 +807,9 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
         const int cy = cell / g.ncx, cx = cell - cy * g.ncx;
         const int cell_y0 = g.ylo + cy * kCellY, cell_x0 = g.xlo + cx * kCellX;
         for (int l = 0; l < g.L && ok; ++l) {
-          const int X0 = (cell_x0 >> l) - RADIUS;
+          const int X0 = ((cell_x0 >> l) - RADIUS) & ~7;
           const int Y0 = (cell_y0 >> l) - RADIUS;
-          const uint32_t box = 128u * g.UW[l] * g.Rg[l];
+          const uint32_t box = 128u * g.UWb[l] * g.Rg[l];
           for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
             const int s = gs % NST;
             const uint32_t use = gs / NST;
@@ -744,6 +842,9 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
             const uint32_t use = gs / NST;
             if (!tc::mbar_wait(bfull + s, use & 1, abort) ||
                 !tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
+            // A rows arrive through cp.async completion: make their
+            // shared-memory writes visible to the tensor core's proxy.
+            tc::fence_proxy_async_smem();
             tc::tc_fence_after();
             const uint32_t sa = base + s * SB;
             const uint32_t sb = sa + 16384;
@@ -790,45 +891,34 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
       const int cell_y0 = g.ylo + ccy * kCellY, cell_x0 = g.xlo + ccx * kCellX;
       for (int l = 0; l < g.L && ok; ++l) {
         const float inv = 1.f / (float)(1 << l);
-        const int rx = (int)floorf(cx * inv) - (cell_x0 >> l);
-        const int ry = (int)floorf(cy * inv) - (cell_y0 >> l);
-        const int UW = g.UW[l], Rg = g.Rg[l];
-        // This pixel's gint row -> per-thread shared scratch (global loads
-        // batched ahead of the shared stores).
-        __half* grow = reinterpret_cast<__half*>(smem + (size_t)NST * SB + 256) +
-                       (size_t)(gb * kTile + t) * g.RDQ;
-        if (valid) {
-          const uint4* src = reinterpret_cast<const uint4*>(p.gint + ((long long)l * g.npix + idx) * g.RDQ);
-          uint4 tmp[(NG * NG + 7) / 8];
-#pragma unroll
-          for (int i = 0; i < (NG * NG + 7) / 8; ++i) tmp[i] = src[i];
-#pragma unroll
-          for (int i = 0; i < (NG * NG + 7) / 8; ++i) reinterpret_cast<uint4*>(grow)[i] = tmp[i];
-        }
+        const int bxl = (int)floorf(cx * inv), byl = (int)floorf(cy * inv);
+        const int ry = byl - (cell_y0 >> l);                          // window row 0 in the box
+        const int X0 = ((cell_x0 >> l) - RADIUS) & ~7;                // box column 0
+        const int cu = (((bxl - RADIUS) & ~7) - X0) >> 3;             // box unit of record unit 0
+        const int UPR = g.UWb[l] >> 3, Rg = g.Rg[l];
+        const uint4* rec = p.gsh + ((long long)l * g.npix + idx) * (NG * NU);
         for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
           if ((int)(gs % (uint32_t)p.nbg) != gb) continue;
           const int s = gs % NST;
           const uint32_t use = gs / NST;
           if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
+          // A row of this pixel: 8 units of 8 K positions (box row br, unit
+          // uc of that row); each a record unit (cp.async) or zeros.
           uint8_t* arow = smem + (size_t)s * SB + t * 128;
+          int br = 0, uc = 0;
 #pragma unroll
-          for (int j = 0; j < 8; ++j)
-            reinterpret_cast<uint4*>(arow)[j ^ (t & 7)] = make_uint4(0, 0, 0, 0);
-          if (valid) {
-            const int u0 = max(gi * Rg, ry), u1 = min(gi * Rg + Rg - 1, ry + RD);
-            for (int U = u0; U <= u1; ++U) {
-              const int jrow = U - ry;
-              const int pos0 = (U - gi * Rg) * UW + rx;
-#pragma unroll
-              for (int k = 0; k < NG; ++k) {
-                const int pos = pos0 + k;
-                *reinterpret_cast<__half*>(arow + (((pos >> 3) ^ (t & 7)) << 4) + (pos & 7) * 2) =
-                    grow[jrow * NG + k];
-              }
-            }
+          for (int k = 0; k < 8; ++k) {
+            const int jj = gi * Rg + br - ry;
+            const int u = uc - cu;
+            uint8_t* dst = arow + ((k ^ (t & 7)) << 4);
+            if (valid && br < Rg && (unsigned)jj < (unsigned)NG && (unsigned)u < (unsigned)NU)
+              tc::cp_async_16(dst, rec + jj * NU + u, 16);
+            else
+              *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+            if (++uc == UPR) { uc = 0; ++br; }
           }
           tc::fence_proxy_async_smem();
-          tc::mbar_arrive(afull + s);
+          tc::cp_async_mbar_arrive_noinc(afull + s);
         }
       }
       if (!ok) break;
@@ -874,6 +964,8 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
 // epilogue adds it to the float32 gradient with red.global.add.v4.f32 (an
 // item may cover only part of Q's cells, so items of one Q add up).
 constexpr int kBwd2Builders = 256;  // builder threads (warps 1..8)
+constexpr int kBwd2Queue = 64;      // kept-pair queue entries per builder warp
+constexpr int kBwd2MaxRanges = 8;   // cell rows per item (rpi <= 16 / 2)
 constexpr int kBwd2Threads = 32 + kBwd2Builders + 128;  // + MMA warp 0, 4 epilogue warps
 
 struct Bwd2Item {
@@ -922,6 +1014,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   __shared__ int abort_flag;
   __shared__ int item_rows;        // rows allocated in the current item
   __shared__ int stage_flags[8];   // bit0: last stage of the item, bit1: item has pixels
+  __shared__ int range_s0[kBwd2MaxRanges], range_n[kBwd2MaxRanges];  // candidate ranges
   const TcGeom& g = p.g;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = p.nstage;
@@ -950,6 +1043,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
+    for (int i = 0; i < 8; ++i) stage_flags[i] = 0;
   }
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -1006,16 +1100,23 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     __syncwarp();
   } else if (warp <= kBwd2Builders / 32) {
     // ---------------- builders ----------------
-    // Kept (pixel, Q) pairs get consecutive rows of the item through one
-    // shared counter; row r of the item goes to stage item_first + r/128.
-    // Each row's A part (its G restricted to Q) is written with plain
-    // stores from registers, its B part (the fmap1 row) by cp.async whose
-    // completion arrives on the stage's afull barrier by itself
-    // (cp.async.mbarrier.arrive.noinc), so no builder waits on its copies.
-    // At the end of an item the closing stage's unused rows are zeroed and
+    // Each builder warp walks its share of the item's candidates (the sorted
+    // ranges of the anchor cells that can reach Q, one flat index space),
+    // with the next batch's base/id loads in flight while it filters the
+    // current one, and queues the kept (pixel, Q) pairs in shared memory.
+    // Every 32 queued pairs it builds 32 consecutive rows of the item: row r
+    // goes to stage item_first + r/128. A row is the pair's G restricted to
+    // Q (8 tile rows x two 16-byte units, each a cp.async of a pre-shifted
+    // record unit or a zero store) and its fmap1 row (cp.async); the copies
+    // arrive on the stage's afull barrier by themselves
+    // (cp.async.mbarrier.arrive.noinc), so no builder waits on a copy. At
+    // the end of an item the closing stage's unused rows are zeroed and
     // arrive too: every stage sees exactly 128 arrivals.
-    constexpr int NGW = (NG * NG + 7) / 8;  // uint4 words of a gint row
+    constexpr int NU = (NG + 14) / 8;
+    constexpr unsigned FULL = 0xffffffffu;
+    const int bw = warp - 1;                 // builder warp 0..7
     const int bt = threadIdx.x - 32;         // builder thread 0..kBwd2Builders-1
+    int4* queue = reinterpret_cast<int4*>(smem + (size_t)NST * SB + 512) + bw * kBwd2Queue;
     uint32_t gs0 = 0, bphase = 0;
     bool ok = true;
     auto bsync = [&]() -> bool {
@@ -1027,110 +1128,129 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       const Bwd2Item item = decode_item(g, it, RADIUS);
       const int l = item.l;
       const int hl = g.h[l], wl = g.w[l];
+      const int nr = item.empty ? 0 : item.rb - item.ra + 1;  // <= kBwd2MaxRanges
+      if (bt < nr) {
+        const long long c0 = (long long)item.b * g.ncell + (long long)(item.ra + bt) * g.ncx + item.ca;
+        const long long c1 = c0 + (item.cb - item.ca);
+        const int s0 = p.offsets[c0];
+        range_s0[bt] = s0;
+        range_n[bt] = p.offsets[c1] + p.counts[c1] - s0;
+      }
       if (bt == 0) item_rows = 0;
       if (!bsync()) { ok = false; break; }
-      const int* sb_l = p.sbase + (long long)l * g.npix;
-      for (int cyr = item.ra; cyr <= item.rb && ok && !item.empty; ++cyr) {
-        const long long c0 = (long long)item.b * g.ncell + (long long)cyr * g.ncx + item.ca;
-        const long long c1 = (long long)item.b * g.ncell + (long long)cyr * g.ncx + item.cb;
-        const int s0 = p.offsets[c0];
-        const int s1 = p.offsets[c1] + p.counts[c1];
-        for (int base = s0; base < s1; base += kBwd2Builders) {
-          const int pos = base + bt;
-          bool touch = false;
-          int x0 = 0, y0 = 0, ylo = 0, yhi = -1, xlo = 0, xhi = -1, gid = 0;
-          if (pos < s1) {
-            const int pk = sb_l[pos];
-            gid = p.sorted[pos];
-            x0 = (int)(short)(pk & 0xFFFF);
-            y0 = pk >> 16;
-            ylo = max(max(y0 - RADIUS, item.qy0), 0);
-            yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
-            xlo = max(max(x0 - RADIUS, item.qx0), 0);
-            xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
-            touch = ylo <= yhi && xlo <= xhi;
-          }
-          const unsigned ballot = __ballot_sync(0xffffffffu, touch);
-          if (ballot == 0) continue;
-          int first = 0;
-          if (lane == 0) first = atomicAdd(&item_rows, __popc(ballot));
-          first = __shfl_sync(0xffffffffu, first, 0);
-          if (!touch) continue;
-          uint4 gr[NGW];
-          {
-            const uint4* src = reinterpret_cast<const uint4*>(
-                p.gint + ((long long)l * g.npix + pos) * g.RDQ);
+      // lane k < nr holds range k and its exclusive prefix
+      const int my_s0 = lane < nr ? range_s0[lane] : 0;
+      const int my_n = lane < nr ? range_n[lane] : 0;
+      int incl = my_n;
 #pragma unroll
-            for (int i = 0; i < NGW; ++i) gr[i] = src[i];
-          }
-          const int r = first + __popc(ballot & lt_mask);
+      for (int o = 1; o < kBwd2MaxRanges; o <<= 1) {
+        const int v = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += v;
+      }
+      const int total = __shfl_sync(FULL, incl, kBwd2MaxRanges - 1);
+      const int my_ex = incl - my_n;
+      auto locate = [&](int f) -> int {
+        int pos = -1;
+        for (int k = 0; k < nr; ++k) {
+          const int e = __shfl_sync(FULL, my_ex, k);
+          const int s0 = __shfl_sync(FULL, my_s0, k);
+          const int n = __shfl_sync(FULL, my_n, k);
+          if (f >= e && f < e + n) pos = s0 + (f - e);
+        }
+        return pos;
+      };
+      const int* sb_l = p.sbase + (long long)l * g.npix;
+      const uint4* gsh_l = p.gsh + (long long)l * g.npix * (NG * NU);
+      int qh = 0, qn = 0;  // queue head and fill (warp-uniform)
+
+      auto build_round = [&](int n) -> bool {
+        const int4 e = queue[(qh + lane) & (kBwd2Queue - 1)];
+        int first = 0;
+        if (lane == 0) first = atomicAdd(&item_rows, n);
+        first = __shfl_sync(FULL, first, 0);
+        bool lok = true;
+        if (lane < n) {
+          const int r = first + lane;
           const uint32_t st = gs0 + (uint32_t)(r / kTile);
           const int row = r % kTile;
           const int s = st % NST;
-          if (!tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort)) { ok = false; continue; }
-          uint8_t* A = smem + (size_t)s * SB;
-          uint8_t* Bm = A + 32768;
-          // (16-byte units are XOR-swizzled by row & 7 everywhere a thread
-          // owns a 128-byte row: rows of a warp then hit distinct banks.)
-#pragma unroll
-          for (int m = 0; m < 2; ++m)
-#pragma unroll
-            for (int j = 0; j < 8; ++j)
-              *reinterpret_cast<uint4*>(A + m * 16384 + row * 128 + ((j ^ (row & 7)) << 4)) =
-                  make_uint4(0, 0, 0, 0);
-          // G restricted to Q. The gint row is parked in this row's own B
-          // bytes (not loaded yet) so the intersection loop can index it;
-          // the fmap1 cp.async below overwrites it after the last read.
-          if (NGW * 16 <= g.KC * 128) {
-#pragma unroll
-            for (int i = 0; i < NGW; ++i)
-              *reinterpret_cast<uint4*>(Bm + (i >> 3) * 16384 + row * 128 + (((i & 7) ^ (row & 7)) << 4)) = gr[i];
-            for (int yy = ylo; yy <= yhi; ++yy) {
-              const int e0 = (yy - (y0 - RADIUS)) * NG - (x0 - RADIUS);
-              const int p0 = (yy - item.qy0) * 16 - item.qx0;
-              for (int xx = xlo; xx <= xhi; ++xx) {
-                const int e = e0 + xx;
-                const unsigned short hb = *reinterpret_cast<const unsigned short*>(
-                    Bm + (e >> 6) * 16384 + row * 128 + (((((e & 63) >> 3) ^ (row & 7))) << 4) +
-                    (e & 7) * 2);
-                const int pq = p0 + xx;
-                const int m = pq >> 6, cc = pq & 63;
-                *reinterpret_cast<unsigned short*>(A + m * 16384 + row * 128 +
-                                                   ((((cc >> 3) ^ (row & 7))) << 4) + (cc & 7) * 2) = hb;
-              }
-            }
+          if (!tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort)) {
+            lok = false;
           } else {
+            uint8_t* A = smem + (size_t)s * SB;
+            uint8_t* Bm = A + 32768;
+            const int x0 = (int)(short)(e.z & 0xFFFF), y0 = e.z >> 16;
+            const uint4* rec = gsh_l + (long long)e.x * (NG * NU);
+            const int dy = item.qy0 - y0 + RADIUS;                    // grid row of tile row 0
+            const int cu = (((x0 - RADIUS) & ~7) - item.qx0) >> 3;    // tile unit of record unit 0
+            const int sw = row & 7;  // 16-byte units XOR-swizzled by row (SW128)
 #pragma unroll
-            for (int jj = 0; jj < NG; ++jj) {
-              const int yy = y0 - RADIUS + jj;
-              const bool rin = yy >= ylo && yy <= yhi;
+            for (int i = 0; i < 8; ++i) {
+              const int jj = i + dy;
+              const bool rv = (unsigned)jj < (unsigned)NG;
 #pragma unroll
-              for (int kk = 0; kk < NG; ++kk) {
-                const int xx = x0 - RADIUS + kk;
-                if (rin && xx >= xlo && xx <= xhi) {
-                  const int e = jj * NG + kk;
-                  const uint4 q4 = gr[e >> 3];
-                  const int wsel = (e & 7) >> 1;
-                  const uint32_t wv = wsel == 0 ? q4.x : wsel == 1 ? q4.y : wsel == 2 ? q4.z : q4.w;
-                  const unsigned short hb = (e & 1) ? (unsigned short)(wv >> 16) : (unsigned short)(wv & 0xFFFF);
-                  const int pq = (yy - item.qy0) * 16 + (xx - item.qx0);
-                  const int m = pq >> 6, cc = pq & 63;
-                  *reinterpret_cast<unsigned short*>(A + m * 16384 + row * 128 +
-                                                     ((((cc >> 3) ^ (row & 7))) << 4) + (cc & 7) * 2) = hb;
-                }
+              for (int d = 0; d < 2; ++d) {
+                const int u = d - cu;
+                uint8_t* dst = A + (i >> 2) * 16384 + row * 128 + (((((i & 3) << 1) | d) ^ sw) << 4);
+                if (rv && (unsigned)u < (unsigned)NU)
+                  tc::cp_async_16(dst, rec + jj * NU + u, 16);
+                else
+                  *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
               }
             }
-          }
-          tc::fence_proxy_async_smem();
-          const __half* f1 = p.fmap1 + (long long)gid * g.C;
-          for (int kc = 0; kc < g.KC; ++kc)
+            tc::fence_proxy_async_smem();
+            const __half* f1 = p.fmap1 + (long long)e.y * g.C;
+            for (int kc = 0; kc < g.KC; ++kc)
 #pragma unroll
-            for (int j = 0; j < 8; ++j)
-              tc::cp_async_16(Bm + kc * 16384 + row * 128 + ((j ^ (row & 7)) << 4),
-                              f1 + kc * 64 + j * 8, 16);
-          tc::cp_async_mbar_arrive_noinc(afull + s);
+              for (int j = 0; j < 8; ++j)
+                tc::cp_async_16(Bm + kc * 16384 + row * 128 + ((j ^ sw) << 4), f1 + kc * 64 + j * 8, 16);
+            tc::cp_async_mbar_arrive_noinc(afull + s);
+          }
+        }
+        return !__any_sync(FULL, !lok);
+      };
+
+      int npos = locate(bw * 32 + lane);
+      int npk = 0, ngid = 0;
+      if (npos >= 0) { npk = sb_l[npos]; ngid = p.sorted[npos]; }
+      for (int fb = bw * 32; fb < total && ok; fb += kBwd2Builders) {
+        const int pos = npos, pk = npk, gid = ngid;
+        npos = locate(fb + kBwd2Builders + lane);
+        if (npos >= 0) { npk = sb_l[npos]; ngid = p.sorted[npos]; }
+        bool touch = false;
+        int x0 = 0, y0 = 0;
+        if (pos >= 0) {
+          x0 = (int)(short)(pk & 0xFFFF);
+          y0 = pk >> 16;
+          const int ylo = max(max(y0 - RADIUS, item.qy0), 0);
+          const int yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
+          const int xlo = max(max(x0 - RADIUS, item.qx0), 0);
+          const int xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
+          touch = ylo <= yhi && xlo <= xhi;
+        }
+        const unsigned ballot = __ballot_sync(FULL, touch);
+        if (touch) {
+          queue[(qh + qn + __popc(ballot & lt_mask)) & (kBwd2Queue - 1)] = make_int4(pos, gid, pk, 0);
+          // the rows of this pair's record that meet Q, and its fmap1 row
+          const int j0 = max(item.qy0 - y0 + RADIUS, 0), j1 = min(item.qy0 + 8 - y0 + RADIUS, NG);
+          tc::prefetch_l2_bulk(gsh_l + (long long)pos * (NG * NU) + j0 * NU, (uint32_t)(j1 - j0) * NU * 16);
+          tc::prefetch_l2_bulk(p.fmap1 + (long long)gid * g.C, (uint32_t)g.C * 2);
+        }
+        qn += __popc(ballot);
+        if (qn >= 32) {
+          __syncwarp();
+          if (!build_round(32)) ok = false;
+          qh += 32;
+          qn -= 32;
         }
       }
+      if (ok && qn > 0) {
+        __syncwarp();
+        if (!build_round(qn)) ok = false;
+        qh += qn;
+        qn = 0;
+      }
+      ok = !__any_sync(FULL, !ok);
       if (!ok) break;
       // Close the item.
       if (!bsync()) { ok = false; break; }
@@ -1250,7 +1370,8 @@ int num_sms() {
 }
 
 struct WsLayout {
-  size_t counts, offsets, keyrank, sorted, inv, work, work_count, sbase, scratch, total;
+  size_t counts, offsets, keyrank, sorted, inv, work, work_count, sbase, scratch, gsh;
+  size_t fwd_total, total;  // bytes the forward / the backward need
   long long max_work;
 };
 
@@ -1269,8 +1390,11 @@ WsLayout ws_layout(const TcGeom& g) {
   w.work = o; o = align256(o + (size_t)w.max_work * 16);
   w.work_count = o; o = align256(o + 4);
   w.sbase = o; o = align256(o + (size_t)g.L * g.npix * 4);
-  w.scratch = o; o = align256(o + (size_t)g.L * g.npix * std::max(g.RDP, g.RDQ) * 2);
-  w.total = o;
+  w.scratch = o; o = align256(o + (size_t)g.L * g.npix * g.RDP * 2);
+  w.fwd_total = o;
+  // the backward's records reuse the forward's output scratch
+  w.gsh = w.scratch;
+  w.total = std::max(o, align256(w.gsh + (size_t)g.L * g.npix * g.NG * g.NU * 16));
   return w;
 }
 
@@ -1284,6 +1408,7 @@ struct TcWs {
   int* work_count;
   int* sbase;
   __half* scratch;
+  uint4* gsh;
 };
 
 TcWs ws_pointers(void* ws, const WsLayout& L) {
@@ -1298,6 +1423,7 @@ TcWs ws_pointers(void* ws, const WsLayout& L) {
   p.work_count = reinterpret_cast<int*>(w + L.work_count);
   p.sbase = reinterpret_cast<int*>(w + L.sbase);
   p.scratch = reinterpret_cast<__half*>(w + L.scratch);
+  p.gsh = reinterpret_cast<uint4*>(w + L.gsh);
   return p;
 }
 
@@ -1371,10 +1497,11 @@ bool tc_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilat
   return eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, nullptr, nullptr);
 }
 
-size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels) {
+size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels, bool backward) {
   TcGeom g;
   if (!make_tc_geom(B, H1, W1, C, radius, levels, &g, nullptr)) return 0;
-  return ws_layout(g).total;
+  const WsLayout L = ws_layout(g);
+  return backward ? L.total : L.fwd_total;
 }
 
 bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1, int W1,
@@ -1388,7 +1515,7 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
     return false;
   }
   const WsLayout L = ws_layout(g);
-  if (ws_bytes < L.total) {
+  if (ws_bytes < L.fwd_total) {
     set_error("tensor-core forward: workspace too small");
     return false;
   }
@@ -1454,6 +1581,9 @@ namespace {
 
 size_t bwd1_stage_bytes(const TcGeom& g) { return 16384 + (size_t)g.KC * 8192; }
 size_t bwd2_stage_bytes(const TcGeom& g) { return 32768 + (size_t)g.KC * 16384; }
+// stages, then 512 B of barriers, then the builder warps' pair queues
+constexpr size_t kBwd2Extra = 512 + (size_t)(kBwd2Builders / 32) * kBwd2Queue * 16;
+size_t bwd2_smem_bytes(int nstage, size_t stage) { return 1024 + (size_t)nstage * stage + kBwd2Extra; }
 
 int pick_stages(size_t stage, size_t extra, int maxst) {
   const size_t lim = (size_t)max_dyn_smem();
@@ -1467,14 +1597,9 @@ bool bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dila
   TcGeom g;
   int nf = 0;
   if (!eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, &g, &nf)) return false;
-  if (g.RDQ == 0) return false;
-  int nbg = 2;
-  int n1 = pick_stages(bwd1_stage_bytes(g), 256 + (size_t)2 * kTile * g.RDQ * 2, 4);
-  if (n1 < 3) {
-    nbg = 1;
-    n1 = pick_stages(bwd1_stage_bytes(g), 256 + (size_t)kTile * g.RDQ * 2, 4);
-  }
-  const int n2 = pick_stages(bwd2_stage_bytes(g), 512, 2);
+  const int nbg = 2;
+  const int n1 = pick_stages(bwd1_stage_bytes(g), 256, 4);
+  const int n2 = pick_stages(bwd2_stage_bytes(g), kBwd2Extra, 4);
   if (n1 < 2 || n2 < 2) {
     if (why) *why = "tensor-core backward shared-memory budget exceeded";
     return false;
@@ -1487,22 +1612,26 @@ bool bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dila
 
 template <int RADIUS>
 bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __half* corr_grad,
-                        const int* inv, __half* gint, float scale, int ymajor, cudaStream_t s) {
+                        const int* inv, uint4* gsh, float scale, int ymajor, cudaStream_t s) {
   const TcGeom& g = p1.g;
   dim3 ug((g.HW + 127) / 128, g.L, g.B);
-  tc_gint_kernel<RADIUS><<<ug, 128, 0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gint,
-                                            const_cast<int*>(p1.sbase), p1.grad_f1, scale,
-                                            ymajor, g);
+  auto k0 = tc_gint_kernel<RADIUS>;
+  const size_t smem0 = GintShape<RADIUS>::smem_bytes;
+  if (!ensure_smem_attr((const void*)k0, smem0)) return false;
+  // 16-byte loads of the incoming gradient rows need HW % 8 == 0 and an
+  // aligned base
+  const int vec_ok = (g.HW % 8 == 0) && (reinterpret_cast<uintptr_t>(corr_grad) % 16 == 0);
+  k0<<<ug, 128, smem0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gsh,
+                            const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, vec_ok, g);
   count_launch();
   if (!check_launch("tc_gint")) return false;
-  const size_t smem1 =
-      1024 + (size_t)p1.nstage * p1.stage_bytes + 256 + (size_t)p1.nbg * kTile * g.RDQ * 2;
+  const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256;
   auto k1 = tc_bwd1_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k1, smem1)) return false;
   k1<<<num_sms(), 64 + 128 * p1.nbg, smem1, s>>>(p1);
   count_launch();
   if (!check_launch("tc_bwd1")) return false;
-  const size_t smem2 = std::max<size_t>(1024 + (size_t)p2.nstage * p2.stage_bytes + 512, 120 * 1024);
+  const size_t smem2 = std::max<size_t>(bwd2_smem_bytes(p2.nstage, p2.stage_bytes), 120 * 1024);
   auto k2 = tc_bwd2_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k2, smem2)) return false;
   k2<<<num_sms(), kBwd2Threads, smem2, s>>>(p2);
@@ -1548,7 +1677,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
     cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)g.w[l], (cuuint64_t)g.h[l], (cuuint64_t)B};
     cuuint64_t strides[3] = {(cuuint64_t)C * 2, (cuuint64_t)g.w[l] * C * 2,
                              (cuuint64_t)g.batch_elems * 2};
-    cuuint32_t box[4] = {64, (cuuint32_t)g.UW[l], (cuuint32_t)g.Rg[l], 1};
+    cuuint32_t box[4] = {64, (cuuint32_t)g.UWb[l], (cuuint32_t)g.Rg[l], 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
     CUresult r = encode(&p1.tmap[l], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, (void*)base, dims,
                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -1566,7 +1695,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.offsets = W.offsets;
   p1.work = W.work;
   p1.work_count = W.work_count;
-  p1.gint = W.scratch;
+  p1.gsh = W.gsh;
   p1.sbase = W.sbase;
   p1.fmap1 = static_cast<const __half*>(f1);
   p1.grad_f1 = static_cast<__half*>(f1g);
@@ -1582,9 +1711,9 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p2.stage_bytes = (uint32_t)bwd2_stage_bytes(g);
   const __half* cg = static_cast<const __half*>(gout);
   switch (radius) {
-    case 3: return launch_bwd_kernels<3>(p1, p2, cg, W.inv, W.scratch, scale, ymajor, s);
-    case 4: return launch_bwd_kernels<4>(p1, p2, cg, W.inv, W.scratch, scale, ymajor, s);
-    case 8: return launch_bwd_kernels<8>(p1, p2, cg, W.inv, W.scratch, scale, ymajor, s);
+    case 3: return launch_bwd_kernels<3>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, s);
+    case 4: return launch_bwd_kernels<4>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, s);
+    case 8: return launch_bwd_kernels<8>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, s);
     default: set_error("radius not instantiated"); return false;
   }
 }
@@ -1670,7 +1799,7 @@ extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
     set_error("no-alloc forward: maps must be 16-byte aligned");
     return false;
   }
-  const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels);
+  const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels, false);
   if (need > LCB200_NOALLOC_SCRATCH_BYTES) {
     set_error("no-alloc forward: this problem needs " + std::to_string(need) +
               " bytes of scratch, more than the fixed " +

@@ -290,8 +290,12 @@ def main(argv=None):
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", default=DEFAULT, choices=sorted(CONFIGS))
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=None,
+                    help="override the per-GPU batch (smaller cases of a workload, for profiling)")
     args = ap.parse_args(argv)
     cfg = dict(CONFIGS[args.config])
+    if args.batch is not None:
+        cfg["B"] = args.batch
     if args.impl == "reference":
         return reference_arm(args, cfg, args.config)
 

@@ -91,7 +91,7 @@ struct TcGeom {
   int UWb[kMaxTcLevels];  // grad_fmap1 box width: 8-aligned origin, multiple of 8
   int Rg[kMaxTcLevels], ngroups[kMaxTcLevels];
   int nqy[kMaxTcLevels], nqx[kMaxTcLevels], rpi[kMaxTcLevels], qgroups[kMaxTcLevels];
-  long long items_before[kMaxTcLevels + 1];  // grad_fmap2 items, coarse levels first
+  long long items_before[kMaxTcLevels + 1];  // grad_fmap2 items of one image, coarse levels first
 };
 
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
@@ -179,7 +179,7 @@ bool make_tc_geom(int B, int H, int W, int C, int r, int L, TcGeom* g, std::stri
   for (int i = 0; i < L; ++i) {
     const int l = L - 1 - i;  // coarse levels first (longest items first)
     t.items_before[i + 1] =
-        t.items_before[i] + (long long)B * t.nqy[l] * t.nqx[l] * t.qgroups[l];
+        t.items_before[i] + (long long)t.nqy[l] * t.nqx[l] * t.qgroups[l];
   }
   *g = t;
   return true;
@@ -974,17 +974,20 @@ struct Bwd2Item {
 };
 
 __device__ __forceinline__ Bwd2Item decode_item(const TcGeom& g, long long it, int radius) {
+  // Items run image by image (the CTAs then share one image's fmap1 rows and
+  // records in L2), coarse levels first within an image (longest first).
   Bwd2Item r{};
+  const long long per_image = g.items_before[g.L];
+  const int b = (int)(it / per_image);
+  long long rem = it - (long long)b * per_image;
   int li = 0;
-  while (li + 1 < g.L && it >= g.items_before[li + 1]) ++li;
+  while (li + 1 < g.L && rem >= g.items_before[li + 1]) ++li;
   const int l = g.L - 1 - li;
-  long long rem = it - g.items_before[li];
+  rem -= g.items_before[li];
   const int grp = (int)(rem % g.qgroups[l]);
   rem /= g.qgroups[l];
   const int qtx = (int)(rem % g.nqx[l]);
-  rem /= g.nqx[l];
-  const int qty = (int)(rem % g.nqy[l]);
-  const int b = (int)(rem / g.nqy[l]);
+  const int qty = (int)(rem / g.nqx[l]);
   r.l = l;
   r.b = b;
   r.qy0 = qty * 8;
@@ -1015,6 +1018,8 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   __shared__ int item_rows;        // rows allocated in the current item
   __shared__ int stage_flags[8];   // bit0: last stage of the item, bit1: item has pixels
   __shared__ int range_s0[kBwd2MaxRanges], range_n[kBwd2MaxRanges];  // candidate ranges
+  __shared__ int left_n;                  // pooled leftover pairs of the current item
+  __shared__ int4 left_q[kBwd2Builders];
   const TcGeom& g = p.g;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = p.nstage;
@@ -1136,7 +1141,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         range_s0[bt] = s0;
         range_n[bt] = p.offsets[c1] + p.counts[c1] - s0;
       }
-      if (bt == 0) item_rows = 0;
+      if (bt == 0) { item_rows = 0; left_n = 0; }
       if (!bsync()) { ok = false; break; }
       // lane k < nr holds range k and its exclusive prefix
       const int my_s0 = lane < nr ? range_s0[lane] : 0;
@@ -1163,51 +1168,61 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       const uint4* gsh_l = p.gsh + (long long)l * g.npix * (NG * NU);
       int qh = 0, qn = 0;  // queue head and fill (warp-uniform)
 
-      auto build_round = [&](int n) -> bool {
-        const int4 e = queue[(qh + lane) & (kBwd2Queue - 1)];
+      // Build one chunk of 32 consecutive rows of the item (the chunk lies in
+      // one stage): lane i < n holds pair e. Each lane writes its row's A
+      // part (record units or zeros; rows past n are all zeros); the fmap1
+      // rows are copied by the whole warp, one contiguous row per
+      // instruction. Every lane then arrives once on the stage's afull
+      // barrier when all of its copies have landed, so a chunk accounts for
+      // 32 of the stage's 128 arrivals.
+      auto build_chunk = [&](const int4 e, int n) -> bool {
         int first = 0;
-        if (lane == 0) first = atomicAdd(&item_rows, n);
+        if (lane == 0) first = atomicAdd(&item_rows, 32);
         first = __shfl_sync(FULL, first, 0);
-        bool lok = true;
-        if (lane < n) {
-          const int r = first + lane;
-          const uint32_t st = gs0 + (uint32_t)(r / kTile);
-          const int row = r % kTile;
-          const int s = st % NST;
-          if (!tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort)) {
-            lok = false;
-          } else {
-            uint8_t* A = smem + (size_t)s * SB;
-            uint8_t* Bm = A + 32768;
-            const int x0 = (int)(short)(e.z & 0xFFFF), y0 = e.z >> 16;
-            const uint4* rec = gsh_l + (long long)e.x * (NG * NU);
-            const int dy = item.qy0 - y0 + RADIUS;                    // grid row of tile row 0
-            const int cu = (((x0 - RADIUS) & ~7) - item.qx0) >> 3;    // tile unit of record unit 0
-            const int sw = row & 7;  // 16-byte units XOR-swizzled by row (SW128)
+        const uint32_t st = gs0 + (uint32_t)(first / kTile);
+        const int s = st % NST;
+        const int row0 = first % kTile;
+        const bool got = tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort);
+        if (__any_sync(FULL, !got)) return false;
+        uint8_t* A = smem + (size_t)s * SB;
+        uint8_t* Bm = A + 32768;
+        const int row = row0 + lane;
+        const int sw = row & 7;  // 16-byte units XOR-swizzled by row (SW128)
+        const int x0 = (int)(short)(e.z & 0xFFFF), y0 = e.z >> 16;
+        const uint4* rec = gsh_l + (long long)e.x * (NG * NU);
+        const int dy = lane < n ? item.qy0 - y0 + RADIUS : -64;      // grid row of tile row 0
+        const int cu = (((x0 - RADIUS) & ~7) - item.qx0) >> 3;        // tile unit of record unit 0
 #pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              const int jj = i + dy;
-              const bool rv = (unsigned)jj < (unsigned)NG;
+        for (int i = 0; i < 8; ++i) {
+          const int jj = i + dy;
+          const bool rv = (unsigned)jj < (unsigned)NG;
 #pragma unroll
-              for (int d = 0; d < 2; ++d) {
-                const int u = d - cu;
-                uint8_t* dst = A + (i >> 2) * 16384 + row * 128 + (((((i & 3) << 1) | d) ^ sw) << 4);
-                if (rv && (unsigned)u < (unsigned)NU)
-                  tc::cp_async_16(dst, rec + jj * NU + u, 16);
-                else
-                  *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
-              }
-            }
-            tc::fence_proxy_async_smem();
-            const __half* f1 = p.fmap1 + (long long)e.y * g.C;
-            for (int kc = 0; kc < g.KC; ++kc)
-#pragma unroll
-              for (int j = 0; j < 8; ++j)
-                tc::cp_async_16(Bm + kc * 16384 + row * 128 + ((j ^ sw) << 4), f1 + kc * 64 + j * 8, 16);
-            tc::cp_async_mbar_arrive_noinc(afull + s);
+          for (int d = 0; d < 2; ++d) {
+            const int u = d - cu;
+            uint8_t* dst = A + (i >> 2) * 16384 + row * 128 + (((((i & 3) << 1) | d) ^ sw) << 4);
+            if (rv && (unsigned)u < (unsigned)NU)
+              tc::cp_async_16(dst, rec + jj * NU + u, 16);
+            else
+              *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
           }
         }
-        return !__any_sync(FULL, !lok);
+        tc::fence_proxy_async_smem();
+        const int U = g.KC * 8;           // 16-byte units of an fmap1 row
+        const int rpi = 32 / U;           // rows per warp instruction
+        const int sub = lane / U, ul = lane - sub * U;
+        const int kc = ul >> 3, j = ul & 7;
+        const bool act = sub < rpi;
+        for (int rr = 0; rr < n; rr += rpi) {
+          const int q = rr + sub;
+          const int gq = __shfl_sync(FULL, e.y, q & 31);
+          if (act && q < n) {
+            const int rq = row0 + q;
+            tc::cp_async_16(Bm + kc * 16384 + rq * 128 + ((j ^ (rq & 7)) << 4),
+                            p.fmap1 + (long long)gq * g.C + kc * 64 + j * 8, 16);
+          }
+        }
+        tc::cp_async_mbar_arrive_noinc(afull + s);
+        return true;
       };
 
       int npos = locate(bw * 32 + lane);
@@ -1239,16 +1254,29 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         qn += __popc(ballot);
         if (qn >= 32) {
           __syncwarp();
-          if (!build_round(32)) ok = false;
+          if (!build_chunk(queue[(qh + lane) & (kBwd2Queue - 1)], 32)) ok = false;
           qh += 32;
           qn -= 32;
         }
       }
-      if (ok && qn > 0) {
-        __syncwarp();
-        if (!build_round(qn)) ok = false;
-        qh += qn;
-        qn = 0;
+      ok = !__any_sync(FULL, !ok);
+      if (!ok) break;
+      // Leftover pairs of all warps (< 32 each) are pooled so that only the
+      // item's last chunk is partly filled.
+      __syncwarp();
+      {
+        int base = 0;
+        if (lane == 0 && qn > 0) base = atomicAdd(&left_n, qn);
+        base = __shfl_sync(FULL, base, 0);
+        if (lane < qn) left_q[base + lane] = queue[(qh + lane) & (kBwd2Queue - 1)];
+      }
+      if (!bsync()) { ok = false; break; }
+      {
+        const int M = left_n;
+        for (int c0 = bw * 32; c0 < M && ok; c0 += kBwd2Builders) {
+          const int n = min(32, M - c0);
+          if (!build_chunk(left_q[c0 + (lane < n ? lane : 0)], n)) ok = false;
+        }
       }
       ok = !__any_sync(FULL, !ok);
       if (!ok) break;
@@ -1701,7 +1729,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.grad_f1 = static_cast<__half*>(f1g);
   p1.grad_f2 = f2g;
   p1.g = g;
-  p1.nitems = g.items_before[levels];
+  p1.nitems = (long long)B * g.items_before[levels];
   TcBwdParams p2 = p1;
   p1.nstage = n1 / 4;
   p1.nbg = n1 % 4;

@@ -1015,11 +1015,11 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   constexpr int NG = RD + 1;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
-  __shared__ int item_rows;        // rows allocated in the current item
+  __shared__ int item_rows[2];     // rows allocated in the current item (by item parity)
   __shared__ int stage_flags[8];   // bit0: last stage of the item, bit1: item has pixels
   __shared__ int range_s0[kBwd2MaxRanges], range_n[kBwd2MaxRanges];  // candidate ranges
-  __shared__ int left_n;                  // pooled leftover pairs of the current item
-  __shared__ int4 left_q[kBwd2Builders];
+  __shared__ int left_n[2];               // pooled leftover pairs (by item parity)
+  __shared__ int4 left_q[2][kBwd2Builders];
   const TcGeom& g = p.g;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = p.nstage;
@@ -1107,16 +1107,19 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     // ---------------- builders ----------------
     // Each builder warp walks its share of the item's candidates (the sorted
     // ranges of the anchor cells that can reach Q, one flat index space),
-    // with the next batch's base/id loads in flight while it filters the
-    // current one, and queues the kept (pixel, Q) pairs in shared memory.
-    // Every 32 queued pairs it builds 32 consecutive rows of the item: row r
-    // goes to stage item_first + r/128. A row is the pair's G restricted to
-    // Q (8 tile rows x two 16-byte units, each a cp.async of a pre-shifted
-    // record unit or a zero store) and its fmap1 row (cp.async); the copies
-    // arrive on the stage's afull barrier by themselves
-    // (cp.async.mbarrier.arrive.noinc), so no builder waits on a copy. At
-    // the end of an item the closing stage's unused rows are zeroed and
-    // arrive too: every stage sees exactly 128 arrivals.
+    // with the base/id loads of the next three batches in flight, and queues
+    // the kept (pixel, Q) pairs in shared memory. Every 32 queued pairs it
+    // builds a chunk of 32 consecutive rows of the item (row r of the item
+    // goes to stage item_first + r/128). A row is the pair's G restricted
+    // to Q (8 tile rows x two 16-byte units, each a cp.async of a
+    // pre-shifted record unit or a zero store) and its fmap1 row (copied by
+    // the whole warp); the copies arrive on the stage's afull barrier by
+    // themselves (cp.async.mbarrier.arrive.noinc), so no builder waits on a
+    // copy. At the end of the scan the warps pool their leftover pairs
+    // (one barrier); the leftover chunks and the zero chunks that complete
+    // the item's last stage then go to fixed rows, and the builders of that
+    // last stage mark it (stage_flags) before arriving: every stage sees
+    // exactly 128 arrivals and the next item starts without another barrier.
     constexpr int NU = (NG + 14) / 8;
     constexpr unsigned FULL = 0xffffffffu;
     const int bw = warp - 1;                 // builder warp 0..7
@@ -1129,7 +1132,8 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       return tc::mbar_wait(bsync_bar, (bphase++) & 1, abort);
     };
     const unsigned lt_mask = (1u << lane) - 1u;
-    for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+    int par = 0;  // item parity: per-item shared state is double-buffered
+    for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, par ^= 1) {
       const Bwd2Item item = decode_item(g, it, RADIUS);
       const int l = item.l;
       const int hl = g.h[l], wl = g.w[l];
@@ -1141,7 +1145,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         range_s0[bt] = s0;
         range_n[bt] = p.offsets[c1] + p.counts[c1] - s0;
       }
-      if (bt == 0) { item_rows = 0; left_n = 0; }
+      if (bt == 0) { item_rows[par] = 0; left_n[par] = 0; }
       if (!bsync()) { ok = false; break; }
       // lane k < nr holds range k and its exclusive prefix
       const int my_s0 = lane < nr ? range_s0[lane] : 0;
@@ -1167,23 +1171,22 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       const int* sb_l = p.sbase + (long long)l * g.npix;
       const uint4* gsh_l = p.gsh + (long long)l * g.npix * (NG * NU);
       int qh = 0, qn = 0;  // queue head and fill (warp-uniform)
+      int cs = -1, cflags = 0;  // the item's last stage (known once the scan is done)
 
-      // Build one chunk of 32 consecutive rows of the item (the chunk lies in
-      // one stage): lane i < n holds pair e. Each lane writes its row's A
-      // part (record units or zeros; rows past n are all zeros); the fmap1
-      // rows are copied by the whole warp, one contiguous row per
-      // instruction. Every lane then arrives once on the stage's afull
-      // barrier when all of its copies have landed, so a chunk accounts for
-      // 32 of the stage's 128 arrivals.
-      auto build_chunk = [&](const int4 e, int n) -> bool {
-        int first = 0;
-        if (lane == 0) first = atomicAdd(&item_rows, 32);
-        first = __shfl_sync(FULL, first, 0);
+      // Build one chunk of 32 consecutive rows of the item starting at row
+      // `first` (the chunk lies in one stage): lane i < n holds pair e. Each
+      // lane writes its row's A part (record units or zeros; rows past n
+      // are all zeros); the fmap1 rows are copied by the whole warp, one
+      // contiguous row per instruction. Every lane then arrives once on the
+      // stage's afull barrier when all of its copies have landed, so a
+      // chunk accounts for 32 of the stage's 128 arrivals.
+      auto build_chunk = [&](const int4 e, int n, int first) -> bool {
         const uint32_t st = gs0 + (uint32_t)(first / kTile);
         const int s = st % NST;
         const int row0 = first % kTile;
         const bool got = tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort);
         if (__any_sync(FULL, !got)) return false;
+        if (lane == 0 && (int)st == cs) stage_flags[s] = cflags;
         uint8_t* A = smem + (size_t)s * SB;
         uint8_t* Bm = A + 32768;
         const int row = row0 + lane;
@@ -1221,17 +1224,24 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
                             p.fmap1 + (long long)gq * g.C + kc * 64 + j * 8, 16);
           }
         }
+        __threadfence_block();  // the stage flag and zero stores before the arrival
         tc::cp_async_mbar_arrive_noinc(afull + s);
         return true;
       };
 
-      int npos = locate(bw * 32 + lane);
-      int npk = 0, ngid = 0;
-      if (npos >= 0) { npk = sb_l[npos]; ngid = p.sorted[npos]; }
+      // candidate loads three batches ahead
+      int pA = locate(bw * 32 + lane), kA = 0, gA = 0;
+      if (pA >= 0) { kA = sb_l[pA]; gA = p.sorted[pA]; }
+      int pB = locate(bw * 32 + kBwd2Builders + lane), kB = 0, gB = 0;
+      if (pB >= 0) { kB = sb_l[pB]; gB = p.sorted[pB]; }
+      int pC = locate(bw * 32 + 2 * kBwd2Builders + lane), kC = 0, gC = 0;
+      if (pC >= 0) { kC = sb_l[pC]; gC = p.sorted[pC]; }
       for (int fb = bw * 32; fb < total && ok; fb += kBwd2Builders) {
-        const int pos = npos, pk = npk, gid = ngid;
-        npos = locate(fb + kBwd2Builders + lane);
-        if (npos >= 0) { npk = sb_l[npos]; ngid = p.sorted[npos]; }
+        const int pos = pA, pk = kA, gid = gA;
+        pA = pB; kA = kB; gA = gB;
+        pB = pC; kB = kC; gB = gC;
+        pC = locate(fb + 3 * kBwd2Builders + lane);
+        if (pC >= 0) { kC = sb_l[pC]; gC = p.sorted[pC]; }
         bool touch = false;
         int x0 = 0, y0 = 0;
         if (pos >= 0) {
@@ -1254,56 +1264,53 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         qn += __popc(ballot);
         if (qn >= 32) {
           __syncwarp();
-          if (!build_chunk(queue[(qh + lane) & (kBwd2Queue - 1)], 32)) ok = false;
+          int first = 0;
+          if (lane == 0) first = atomicAdd(&item_rows[par], 32);
+          first = __shfl_sync(FULL, first, 0);
+          if (!build_chunk(queue[(qh + lane) & (kBwd2Queue - 1)], 32, first)) ok = false;
           qh += 32;
           qn -= 32;
         }
       }
       ok = !__any_sync(FULL, !ok);
       if (!ok) break;
-      // Leftover pairs of all warps (< 32 each) are pooled so that only the
-      // item's last chunk is partly filled.
+      // Pool the warps' leftover pairs (< 32 each).
       __syncwarp();
       {
         int base = 0;
-        if (lane == 0 && qn > 0) base = atomicAdd(&left_n, qn);
+        if (lane == 0 && qn > 0) base = atomicAdd(&left_n[par], qn);
         base = __shfl_sync(FULL, base, 0);
-        if (lane < qn) left_q[base + lane] = queue[(qh + lane) & (kBwd2Queue - 1)];
+        if (lane < qn) left_q[par][base + lane] = queue[(qh + lane) & (kBwd2Queue - 1)];
       }
       if (!bsync()) { ok = false; break; }
-      {
-        const int M = left_n;
-        for (int c0 = bw * 32; c0 < M && ok; c0 += kBwd2Builders) {
-          const int n = min(32, M - c0);
-          if (!build_chunk(left_q[c0 + (lane < n ? lane : 0)], n)) ok = false;
+      // Every scan chunk is allocated now: the leftover chunks take rows
+      // [T0, T), then zero chunks complete the last stage cs (an extra zero
+      // stage when the scan filled whole stages and nothing is left over).
+      const int T0 = item_rows[par];
+      const int M = left_n[par];
+      const int NL = (M + 31) / 32;
+      const int T = T0 + 32 * NL;
+      int fill;
+      if (T > 0 && !(NL == 0 && T % kTile == 0)) {
+        cs = (int)gs0 + (T - 1) / kTile;
+        fill = T - (cs - (int)gs0) * kTile;
+      } else {
+        cs = (int)gs0 + T / kTile;
+        fill = 0;
+      }
+      cflags = 1 | (T > 0 ? 2 : 0);
+      const int NP = (kTile - fill) / 32;
+      for (int c = bw; c < NL + NP && ok; c += kBwd2Builders / 32) {
+        if (c < NL) {
+          const int n = min(32, M - 32 * c);
+          if (!build_chunk(left_q[par][32 * c + (lane < n ? lane : 0)], n, T0 + 32 * c)) ok = false;
+        } else {
+          const int first = (cs - (int)gs0) * kTile + fill + 32 * (c - NL);
+          if (!build_chunk(make_int4(0, 0, 0, 0), 0, first)) ok = false;
         }
       }
       ok = !__any_sync(FULL, !ok);
-      if (!ok) break;
-      // Close the item.
-      if (!bsync()) { ok = false; break; }
-      const int T = item_rows;
-      const uint32_t cs = gs0 + (uint32_t)(T / kTile);
-      const int fill = T % kTile;
-      const int s = cs % NST;
-      if (bt == 0) {
-        if (!tc::mbar_wait(empty + s, ((cs / NST) & 1) ^ 1, abort)) ok = false;
-        else stage_flags[s] = 1 | (T > 0 ? 2 : 0);
-      }
-      if (!bsync() || !ok) { ok = false; break; }
-      if (bt < kTile && bt >= fill) {
-        if (!tc::mbar_wait(empty + s, ((cs / NST) & 1) ^ 1, abort)) { ok = false; break; }
-        uint8_t* A = smem + (size_t)s * SB;
-#pragma unroll
-        for (int m = 0; m < 2; ++m)
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            *reinterpret_cast<uint4*>(A + m * 16384 + bt * 128 + ((j ^ (bt & 7)) << 4)) =
-                make_uint4(0, 0, 0, 0);
-        tc::fence_proxy_async_smem();
-        tc::mbar_arrive(afull + s);
-      }
-      gs0 = cs + 1;
+      gs0 = (uint32_t)cs + 1;
     }
     // Copies still in flight complete before the kernel's final barrier.
     tc::cp_async_wait_all();

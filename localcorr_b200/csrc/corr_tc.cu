@@ -1254,13 +1254,8 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           touch = ylo <= yhi && xlo <= xhi;
         }
         const unsigned ballot = __ballot_sync(FULL, touch);
-        if (touch) {
+        if (touch)
           queue[(qh + qn + __popc(ballot & lt_mask)) & (kBwd2Queue - 1)] = make_int4(pos, gid, pk, 0);
-          // the rows of this pair's record that meet Q, and its fmap1 row
-          const int j0 = max(item.qy0 - y0 + RADIUS, 0), j1 = min(item.qy0 + 8 - y0 + RADIUS, NG);
-          tc::prefetch_l2_bulk(gsh_l + (long long)pos * (NG * NU) + j0 * NU, (uint32_t)(j1 - j0) * NU * 16);
-          tc::prefetch_l2_bulk(p.fmap1 + (long long)gid * g.C, (uint32_t)g.C * 2);
-        }
         qn += __popc(ballot);
         if (qn >= 32) {
           __syncwarp();

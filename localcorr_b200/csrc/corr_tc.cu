@@ -52,6 +52,7 @@ __device__ int g_tc_status = 0;
 namespace {
 
 constexpr int kCellY = 8, kCellX = 16, kTile = 128;
+constexpr int kColBins = kCellX;  // sort bins per cell: the level-0 base column in the cell
 constexpr int kMaxTcLevels = 4;
 constexpr int kBwd1Threads = 64 + 256;  // grad_fmap1: producer, MMA, 2 x 4 builder warps
 constexpr int kFwdEG = 3;          // forward epilogue warp groups
@@ -218,15 +219,19 @@ __global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ 
   if (fx >= (float)g.xlo && fx < (float)g.xhi && fy >= (float)g.ylo && fy < (float)g.yhi) {
     const int bx = (int)fx, by = (int)fy;
     const int cell = ((by - g.ylo) / kCellY) * g.ncx + (bx - g.xlo) / kCellX;
-    kr.x = cell;
-    kr.y = atomicAdd(counts + (long long)b * g.ncell + cell, 1);
+    const int key = cell * kColBins + (bx - g.xlo) % kCellX;  // (cell, column in cell)
+    kr.x = key;
+    kr.y = atomicAdd(counts + (long long)b * g.ncell * kColBins + key, 1);
   }
   keyrank[gid] = kr;
 }
 
-// One CTA: exclusive scan of the per-cell counts (cell offsets into the
-// sorted order) and of the per-cell chunk counts (work-list offsets), then
-// the work list itself: {b, cell, first sorted index, pixel count <= 128}.
+// One CTA: exclusive scan over the cells of the per-cell counts (a cell's
+// count is the sum of its column bins) and of the per-cell chunk counts
+// (work-list offsets); writes the offsets of every (cell, column) bin into
+// the sorted order (bins in order, so a cell's pixels are sorted by their
+// base column), a final entry = number of sorted pixels, and the work list:
+// {b, cell, first sorted index, pixel count <= 128}.
 __global__ void __launch_bounds__(1024)
 tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
                int4* __restrict__ work, int* __restrict__ work_count, int ncell_total,
@@ -238,7 +243,18 @@ tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
   __syncthreads();
   for (int base = 0; base < ncell_total; base += 1024) {
     const int i = base + threadIdx.x;
-    const int cnt = i < ncell_total ? counts[i] : 0;
+    int bins[kColBins];
+    int cnt = 0;
+    if (i < ncell_total) {
+      const int4* src = reinterpret_cast<const int4*>(counts + (long long)i * kColBins);
+#pragma unroll
+      for (int q = 0; q < kColBins / 4; ++q) {
+        const int4 v = src[q];
+        bins[4 * q] = v.x; bins[4 * q + 1] = v.y; bins[4 * q + 2] = v.z; bins[4 * q + 3] = v.w;
+      }
+#pragma unroll
+      for (int q = 0; q < kColBins; ++q) cnt += bins[q];
+    }
     const int nch = (cnt + kTile - 1) / kTile;
     int2 in = make_int2(cnt, nch), ex, tot;
     // Scan both values with a pair-sum operator.
@@ -247,7 +263,17 @@ tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
     const int off = carry[0] + ex.x;
     const int coff = carry[1] + ex.y;
     if (i < ncell_total) {
-      offsets[i] = off;
+      int run = off;
+      int4* dst = reinterpret_cast<int4*>(offsets + (long long)i * kColBins);
+#pragma unroll
+      for (int q = 0; q < kColBins / 4; ++q) {
+        int4 v;
+        v.x = run; run += bins[4 * q];
+        v.y = run; run += bins[4 * q + 1];
+        v.z = run; run += bins[4 * q + 2];
+        v.w = run; run += bins[4 * q + 3];
+        dst[q] = v;
+      }
       const int b = i / ncell;
       const int cell = i - b * ncell;
       for (int j = 0; j < nch; ++j)
@@ -257,7 +283,10 @@ tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
     if (threadIdx.x == 0) { carry[0] += tot.x; carry[1] += tot.y; }
     __syncthreads();
   }
-  if (threadIdx.x == 0) *work_count = carry[1];
+  if (threadIdx.x == 0) {
+    *work_count = carry[1];
+    offsets[(long long)ncell_total * kColBins] = carry[0];
+  }
 }
 
 __global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* __restrict__ offsets,
@@ -270,9 +299,27 @@ __global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* _
     return;
   }
   const int b = (int)(gid / g.HW);
-  const int pos = offsets[(long long)b * g.ncell + kr.x] + kr.y;
+  const int pos = offsets[(long long)b * g.ncell * kColBins + kr.x] + kr.y;
   sorted[pos] = (int)gid;
   inv[gid] = pos;
+}
+
+// Sorted copy of fmap1 for the grad_fmap2 pull: row i = fmap1 row sorted[i]
+// for the sorted pixels, zeros for the rows past them (their A rows are zero
+// but the TMA tiles read them). One warp per row.
+__global__ void tc_gather_rows_kernel(const __half* __restrict__ fmap1, const int* __restrict__ sorted,
+                                      const int* __restrict__ nsorted, __half* __restrict__ f1s,
+                                      TcGeom g) {
+  const long long row = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= g.npix) return;
+  uint4* dst = reinterpret_cast<uint4*>(f1s + row * g.C);
+  if (row < *nsorted) {
+    const uint4* src = reinterpret_cast<const uint4*>(fmap1 + (long long)sorted[row] * g.C);
+    for (int i = lane; i < g.C / 8; i += 32) dst[i] = src[i];
+  } else {
+    for (int i = lane; i < g.C / 8; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -707,6 +754,7 @@ tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ co
 
 struct alignas(64) TcBwdParams {
   CUtensorMap tmap[kMaxTcLevels];
+  CUtensorMap tmap_f1s;  // sorted fmap1 copy [npix rows][C], 64-channel x 64-row SW128 boxes
   const void* coords;
   const int* sorted;
   const int* counts;
@@ -957,19 +1005,25 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
 // grad_fmap2, pulled per output tile Q of 8x16 level-l positions:
 //   D[128 pos x C] = sum over the pixels whose windows reach Q of
 //                    G^T[pos x px] * fmap1[px x C]
-// The candidate pixels are the contiguous sorted ranges of the anchor cells
-// that can reach Q; builders keep those whose window intersects Q, writing
-// per kept pixel one row of A (MN-major: 128 position weights) and one row of
-// B (MN-major: the fmap1 row, cp.async). D is double-buffered in TMEM; the
-// epilogue adds it to the float32 gradient with red.global.add.v4.f32 (an
-// item may cover only part of Q's cells, so items of one Q add up).
-constexpr int kBwd2Builders = 256;  // builder threads (warps 1..8)
-constexpr int kBwd2Queue = 64;      // kept-pair queue entries per builder warp
-constexpr int kBwd2MaxRanges = 8;   // cell rows per item (rpi <= 16 / 2)
-constexpr int kBwd2Threads = 32 + kBwd2Builders + 128;  // + MMA warp 0, 4 epilogue warps
+// The candidates of an item are, per anchor-cell row, one contiguous range
+// of the sorted order: the cells are sorted by (cell, level-0 base column
+// within the cell), so the columns of the boundary cells whose bases can
+// reach Q are a sub-range and a cell row's candidates are one range. Every
+// candidate is a K row (non-touching ones get an all-zero A row): A rows
+// (MN-major, the pixel's G restricted to Q) are built by the builders from
+// the pre-shifted records with cp.async, B rows are the candidates' fmap1
+// rows, loaded by TMA as 64-row tiles of the sorted fmap1 copy. D is
+// double-buffered in TMEM; the epilogue adds it to the float32 gradient with
+// red.global.add.v4.f32 (items may cover only part of Q's cells).
+constexpr int kB2Rows = 64;                       // K rows per stage
+constexpr int kBwd2Builders = 256;                // builder threads (warps 2..9)
+constexpr int kB2Groups = kBwd2Builders / kB2Rows;  // stage gs is built by group gs % 4
+constexpr int kBwd2MaxRanges = 8;                 // cell rows per item (rpi <= 16 / 2)
+constexpr int kBwd2Threads = 64 + kBwd2Builders + 128;  // MMA warp, TMA warp, builders, epilogue
 
 struct Bwd2Item {
   int l, b, qy0, qx0, ra, rb, ca, cb;  // level, batch, tile origin, cell rows/cols
+  int bx_lo, bx_hi;                    // level-0 base columns that can reach Q
   bool empty;
 };
 
@@ -1005,33 +1059,43 @@ __device__ __forceinline__ Bwd2Item decode_item(const TcGeom& g, long long it, i
   ra = ra + grp * g.rpi[l];
   rb = min(rb, ra + g.rpi[l] - 1);
   r.ra = ra; r.rb = rb; r.ca = ca; r.cb = cb;
+  r.bx_lo = bx_lo; r.bx_hi = bx_hi;
   r.empty = ra > rb || ca > cb;
   return r;
+}
+
+// Sorted range [s0, s1) of the item's candidates in cell row k (k < nranges).
+__device__ __forceinline__ int2 item_range(const TcGeom& g, const int* __restrict__ fine_off,
+                                           const Bwd2Item& it, int k) {
+  const int cyr = it.ra + k;
+  const long long row0 = ((long long)it.b * g.ncell + (long long)cyr * g.ncx) * kColBins;
+  const int la = max(0, it.bx_lo - (g.xlo + it.ca * kCellX));
+  const int lb = min(kColBins - 1, it.bx_hi - (g.xlo + it.cb * kCellX));
+  const int s0 = fine_off[row0 + (long long)it.ca * kColBins + la];
+  const int s1 = fine_off[row0 + (long long)it.cb * kColBins + lb + 1];
+  return make_int2(s0, max(s0, s1));
 }
 
 template <int RADIUS>
 __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_constant__ TcBwdParams p) {
   constexpr int RD = 2 * RADIUS + 1;
   constexpr int NG = RD + 1;
+  constexpr int NU = (NG + 14) / 8;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
-  __shared__ int item_rows[2];     // rows allocated in the current item (by item parity)
-  __shared__ int stage_flags[8];   // bit0: last stage of the item, bit1: item has pixels
-  __shared__ int range_s0[kBwd2MaxRanges], range_n[kBwd2MaxRanges];  // candidate ranges
-  __shared__ int left_n[2];               // pooled leftover pairs (by item parity)
-  __shared__ int4 left_q[2][kBwd2Builders];
+  __shared__ int stage_flags[8];   // 1: last stage of its item
   const TcGeom& g = p.g;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = p.nstage;
-  const uint32_t SB = p.stage_bytes;  // A: 2 x 16 KB, B: KC x 16 KB
+  const uint32_t SB = p.stage_bytes;  // A: 2 x 8 KB (position halves), B: KC x 8 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * SB);
   uint64_t* afull = bars;
-  uint64_t* empty = bars + NST;
-  uint64_t* acc_full = bars + 2 * NST;   // [2]
+  uint64_t* bfull = bars + NST;
+  uint64_t* empty = bars + 2 * NST;
+  uint64_t* acc_full = bars + 3 * NST;   // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
-  uint64_t* bsync_bar = acc_full + 4;    // builder-wide bounded sync
-  uint64_t* fin_bar = acc_full + 5;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 6);
+  uint64_t* fin_bar = acc_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -1040,11 +1104,11 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   tc::fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
-      tc::mbar_init(afull + s, kTile);
+      tc::mbar_init(afull + s, kB2Rows);
+      tc::mbar_init(bfull + s, 1);
       tc::mbar_init(empty + s, 1);
     }
     for (int i = 0; i < 2; ++i) { tc::mbar_init(acc_full + i, 1); tc::mbar_init(acc_empty + i, kTile); }
-    tc::mbar_init(bsync_bar, kBwd2Builders);
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -1060,6 +1124,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   const uint32_t tmem = *tmem_slot;
   volatile int* abort = &abort_flag;
   const long long nitems = p.nitems;
+  const uint32_t bbytes = (uint32_t)g.KC * kB2Rows * 128;
 
   if (warp == 0) {
     // ---------------- MMA issuer ----------------
@@ -1076,19 +1141,20 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         for (;;) {
           const int s = gs % NST;
           const uint32_t use = gs / NST;
-          if (!tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
-          // Rows arrive through cp.async completion: make their shared-memory
-          // writes visible to the tensor core's (async) proxy.
+          if (!tc::mbar_wait(bfull + s, use & 1, abort) ||
+              !tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
+          // A rows arrive through cp.async completion: make their
+          // shared-memory writes visible to the tensor core's proxy.
           tc::fence_proxy_async_smem();
           tc::tc_fence_after();
           const int flags = stage_flags[s];
           stage_flags[s] = 0;
           const uint32_t sa = base + s * SB;
-          const uint32_t sb = sa + 32768;
+          const uint32_t sb = sa + 2 * kB2Rows * 128;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t ad = tc::smem_desc_sw128(sa + kk * 2048, 16384, 1024);
-            const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, 16384, 1024);
+          for (int kk = 0; kk < kB2Rows / 16; ++kk) {
+            const uint64_t ad = tc::smem_desc_sw128(sa + kk * 2048, kB2Rows * 128, 1024);
+            const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, kB2Rows * 128, 1024);
             tc::mma_f16_ss(tmem + buf * 256, ad, bd, idesc, first ? 0u : 1u);
             first = false;
           }
@@ -1103,209 +1169,114 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       tc::mbar_wait(fin_bar, 0, abort);
     }
     __syncwarp();
-  } else if (warp <= kBwd2Builders / 32) {
+  } else if (warp == 1) {
+    // ---------------- TMA producer: B = 64-row tiles of sorted fmap1 ----------------
+    // Same stage sequence as the builders: the item's ranges cut into 64-row
+    // stages (one all-zero stage for an item without candidates). Rows past
+    // a range's end belong to other cells (or are zero fill past the end);
+    // their A rows are zero.
+    if (lane == 0) {
+      uint32_t gs = 0;
+      bool ok = true;
+      for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+        const Bwd2Item item = decode_item(g, it, RADIUS);
+        const int nr = item.empty ? 0 : item.rb - item.ra + 1;
+        int2 rgs[kBwd2MaxRanges];
+        int total_st = 0;
+#pragma unroll
+        for (int k = 0; k < kBwd2MaxRanges; ++k) {
+          rgs[k] = make_int2(0, 0);
+          if (k < nr) {
+            rgs[k] = item_range(g, p.offsets, item, k);
+            total_st += (rgs[k].y - rgs[k].x + kB2Rows - 1) / kB2Rows;
+          }
+        }
+        const int last = max(total_st, 1) - 1;
+        int k = 0, j = 0;
+        for (int q = 0; q <= last && ok; ++q, ++gs) {
+          while (k < nr && j * kB2Rows >= rgs[k].y - rgs[k].x) { ++k; j = 0; }
+          const int row = (k < nr ? rgs[k].x : 0) + (j++) * kB2Rows;
+          const int s = gs % NST;
+          const uint32_t use = gs / NST;
+          if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
+          tc::mbar_arrive_expect_tx(bfull + s, bbytes);
+          uint8_t* sb = smem + (size_t)s * SB + 2 * kB2Rows * 128;
+          for (int kc = 0; kc < g.KC; ++kc)
+            tc::tma_load_2d(sb + kc * kB2Rows * 128, &p.tmap_f1s, bfull + s, kc * 64, row);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp < 2 + kBwd2Builders / 32) {
     // ---------------- builders ----------------
-    // Each builder warp walks its share of the item's candidates (the sorted
-    // ranges of the anchor cells that can reach Q, one flat index space),
-    // with the base/id loads of the next three batches in flight, and queues
-    // the kept (pixel, Q) pairs in shared memory. Every 32 queued pairs it
-    // builds a chunk of 32 consecutive rows of the item (row r of the item
-    // goes to stage item_first + r/128). A row is the pair's G restricted
-    // to Q (8 tile rows x two 16-byte units, each a cp.async of a
-    // pre-shifted record unit or a zero store) and its fmap1 row (copied by
-    // the whole warp); the copies arrive on the stage's afull barrier by
-    // themselves (cp.async.mbarrier.arrive.noinc), so no builder waits on a
-    // copy. At the end of the scan the warps pool their leftover pairs
-    // (one barrier); the leftover chunks and the zero chunks that complete
-    // the item's last stage then go to fixed rows, and the builders of that
-    // last stage mark it (stage_flags) before arriving: every stage sees
-    // exactly 128 arrivals and the next item starts without another barrier.
-    constexpr int NU = (NG + 14) / 8;
-    constexpr unsigned FULL = 0xffffffffu;
-    const int bw = warp - 1;                 // builder warp 0..7
-    const int bt = threadIdx.x - 32;         // builder thread 0..kBwd2Builders-1
-    int4* queue = reinterpret_cast<int4*>(smem + (size_t)NST * SB + 512) + bw * kBwd2Queue;
-    uint32_t gs0 = 0, bphase = 0;
+    // Group gb (two warps, one thread per row) builds the A tiles of the
+    // stages with gs % 4 == gb: row t is candidate s0 + 64 j + t of the
+    // stage's range, its G restricted to Q as 8 tile rows x two 16-byte
+    // units, each a cp.async of a pre-shifted record unit or zeros (rows
+    // past the range and non-touching candidates come out all zero). The
+    // copies arrive on afull by themselves (cp.async.mbarrier.arrive.noinc);
+    // the builder of an item's last stage marks it for the MMA issuer.
+    const int bt = threadIdx.x - 64;
+    const int gb = bt / kB2Rows;
+    const int t = bt % kB2Rows;
+    uint32_t gs = 0;
     bool ok = true;
-    auto bsync = [&]() -> bool {
-      tc::mbar_arrive(bsync_bar);
-      return tc::mbar_wait(bsync_bar, (bphase++) & 1, abort);
-    };
-    const unsigned lt_mask = (1u << lane) - 1u;
-    int par = 0;  // item parity: per-item shared state is double-buffered
-    for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, par ^= 1) {
+    for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
       const Bwd2Item item = decode_item(g, it, RADIUS);
       const int l = item.l;
-      const int hl = g.h[l], wl = g.w[l];
-      const int nr = item.empty ? 0 : item.rb - item.ra + 1;  // <= kBwd2MaxRanges
-      if (bt < nr) {
-        const long long c0 = (long long)item.b * g.ncell + (long long)(item.ra + bt) * g.ncx + item.ca;
-        const long long c1 = c0 + (item.cb - item.ca);
-        const int s0 = p.offsets[c0];
-        range_s0[bt] = s0;
-        range_n[bt] = p.offsets[c1] + p.counts[c1] - s0;
-      }
-      if (bt == 0) { item_rows[par] = 0; left_n[par] = 0; }
-      if (!bsync()) { ok = false; break; }
-      // lane k < nr holds range k and its exclusive prefix
-      const int my_s0 = lane < nr ? range_s0[lane] : 0;
-      const int my_n = lane < nr ? range_n[lane] : 0;
-      int incl = my_n;
+      const int nr = item.empty ? 0 : item.rb - item.ra + 1;
+      int2 rgs[kBwd2MaxRanges];
+      int total_st = 0;
 #pragma unroll
-      for (int o = 1; o < kBwd2MaxRanges; o <<= 1) {
-        const int v = __shfl_up_sync(FULL, incl, o);
-        if (lane >= o) incl += v;
-      }
-      const int total = __shfl_sync(FULL, incl, kBwd2MaxRanges - 1);
-      const int my_ex = incl - my_n;
-      auto locate = [&](int f) -> int {
-        int pos = -1;
-        for (int k = 0; k < nr; ++k) {
-          const int e = __shfl_sync(FULL, my_ex, k);
-          const int s0 = __shfl_sync(FULL, my_s0, k);
-          const int n = __shfl_sync(FULL, my_n, k);
-          if (f >= e && f < e + n) pos = s0 + (f - e);
+      for (int k = 0; k < kBwd2MaxRanges; ++k) {
+        rgs[k] = make_int2(0, 0);
+        if (k < nr) {
+          rgs[k] = item_range(g, p.offsets, item, k);
+          total_st += (rgs[k].y - rgs[k].x + kB2Rows - 1) / kB2Rows;
         }
-        return pos;
-      };
+      }
+      const int last = max(total_st, 1) - 1;
       const int* sb_l = p.sbase + (long long)l * g.npix;
       const uint4* gsh_l = p.gsh + (long long)l * g.npix * (NG * NU);
-      int qh = 0, qn = 0;  // queue head and fill (warp-uniform)
-      int cs = -1, cflags = 0;  // the item's last stage (known once the scan is done)
-
-      // Build one chunk of 32 consecutive rows of the item starting at row
-      // `first` (the chunk lies in one stage): lane i < n holds pair e. Each
-      // lane writes its row's A part (record units or zeros; rows past n
-      // are all zeros); the fmap1 rows are copied by the whole warp, one
-      // contiguous row per instruction. Every lane then arrives once on the
-      // stage's afull barrier when all of its copies have landed, so a
-      // chunk accounts for 32 of the stage's 128 arrivals.
-      auto build_chunk = [&](const int4 e, int n, int first) -> bool {
-        const uint32_t st = gs0 + (uint32_t)(first / kTile);
-        const int s = st % NST;
-        const int row0 = first % kTile;
-        const bool got = tc::mbar_wait(empty + s, ((st / NST) & 1) ^ 1, abort);
-        if (__any_sync(FULL, !got)) return false;
-        if (lane == 0 && (int)st == cs) stage_flags[s] = cflags;
+      int k = 0, j = 0;  // range and stage within it of item stage q
+      for (int q = 0; q <= last && ok; ++q, ++gs) {
+        while (k < nr && j * kB2Rows >= rgs[k].y - rgs[k].x) { ++k; j = 0; }
+        const int s0 = k < nr ? rgs[k].x : 0;
+        const int s1 = k < nr ? rgs[k].y : 0;
+        const int jj0 = j++;
+        if ((int)(gs % kB2Groups) != gb) continue;
+        const int pos = s0 + jj0 * kB2Rows + t;
+        const bool valid = pos < s1;
+        int pk = 0;
+        if (valid) pk = sb_l[pos];
+        const int s = gs % NST;
+        const uint32_t use = gs / NST;
+        if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
+        if (t == 0 && q == last) stage_flags[s] = 1;
         uint8_t* A = smem + (size_t)s * SB;
-        uint8_t* Bm = A + 32768;
-        const int row = row0 + lane;
-        const int sw = row & 7;  // 16-byte units XOR-swizzled by row (SW128)
-        const int x0 = (int)(short)(e.z & 0xFFFF), y0 = e.z >> 16;
-        const uint4* rec = gsh_l + (long long)e.x * (NG * NU);
-        const int dy = lane < n ? item.qy0 - y0 + RADIUS : -64;      // grid row of tile row 0
+        const int sw = t & 7;  // 16-byte units XOR-swizzled by row (SW128)
+        const int x0 = (int)(short)(pk & 0xFFFF), y0 = pk >> 16;
+        const uint4* rec = gsh_l + (long long)pos * (NG * NU);
+        const int dy = valid ? item.qy0 - y0 + RADIUS : -64;          // grid row of tile row 0
         const int cu = (((x0 - RADIUS) & ~7) - item.qx0) >> 3;        // tile unit of record unit 0
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int jj = i + dy;
-          const bool rv = (unsigned)jj < (unsigned)NG;
+          const int jr = i + dy;
+          const bool rv = (unsigned)jr < (unsigned)NG;
 #pragma unroll
           for (int d = 0; d < 2; ++d) {
             const int u = d - cu;
-            uint8_t* dst = A + (i >> 2) * 16384 + row * 128 + (((((i & 3) << 1) | d) ^ sw) << 4);
+            uint8_t* dst = A + (i >> 2) * (kB2Rows * 128) + t * 128 + (((((i & 3) << 1) | d) ^ sw) << 4);
             if (rv && (unsigned)u < (unsigned)NU)
-              tc::cp_async_16(dst, rec + jj * NU + u, 16);
+              tc::cp_async_16(dst, rec + jr * NU + u, 16);
             else
               *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
           }
         }
         tc::fence_proxy_async_smem();
-        const int U = g.KC * 8;           // 16-byte units of an fmap1 row
-        const int rpi = 32 / U;           // rows per warp instruction
-        const int sub = lane / U, ul = lane - sub * U;
-        const int kc = ul >> 3, j = ul & 7;
-        const bool act = sub < rpi;
-        for (int rr = 0; rr < n; rr += rpi) {
-          const int q = rr + sub;
-          const int gq = __shfl_sync(FULL, e.y, q & 31);
-          if (act && q < n) {
-            const int rq = row0 + q;
-            tc::cp_async_16(Bm + kc * 16384 + rq * 128 + ((j ^ (rq & 7)) << 4),
-                            p.fmap1 + (long long)gq * g.C + kc * 64 + j * 8, 16);
-          }
-        }
         __threadfence_block();  // the stage flag and zero stores before the arrival
         tc::cp_async_mbar_arrive_noinc(afull + s);
-        return true;
-      };
-
-      // candidate loads three batches ahead
-      int pA = locate(bw * 32 + lane), kA = 0, gA = 0;
-      if (pA >= 0) { kA = sb_l[pA]; gA = p.sorted[pA]; }
-      int pB = locate(bw * 32 + kBwd2Builders + lane), kB = 0, gB = 0;
-      if (pB >= 0) { kB = sb_l[pB]; gB = p.sorted[pB]; }
-      int pC = locate(bw * 32 + 2 * kBwd2Builders + lane), kC = 0, gC = 0;
-      if (pC >= 0) { kC = sb_l[pC]; gC = p.sorted[pC]; }
-      for (int fb = bw * 32; fb < total && ok; fb += kBwd2Builders) {
-        const int pos = pA, pk = kA, gid = gA;
-        pA = pB; kA = kB; gA = gB;
-        pB = pC; kB = kC; gB = gC;
-        pC = locate(fb + 3 * kBwd2Builders + lane);
-        if (pC >= 0) { kC = sb_l[pC]; gC = p.sorted[pC]; }
-        bool touch = false;
-        int x0 = 0, y0 = 0;
-        if (pos >= 0) {
-          x0 = (int)(short)(pk & 0xFFFF);
-          y0 = pk >> 16;
-          const int ylo = max(max(y0 - RADIUS, item.qy0), 0);
-          const int yhi = min(min(y0 + RADIUS + 1, item.qy0 + 7), hl - 1);
-          const int xlo = max(max(x0 - RADIUS, item.qx0), 0);
-          const int xhi = min(min(x0 + RADIUS + 1, item.qx0 + 15), wl - 1);
-          touch = ylo <= yhi && xlo <= xhi;
-        }
-        const unsigned ballot = __ballot_sync(FULL, touch);
-        if (touch)
-          queue[(qh + qn + __popc(ballot & lt_mask)) & (kBwd2Queue - 1)] = make_int4(pos, gid, pk, 0);
-        qn += __popc(ballot);
-        if (qn >= 32) {
-          __syncwarp();
-          int first = 0;
-          if (lane == 0) first = atomicAdd(&item_rows[par], 32);
-          first = __shfl_sync(FULL, first, 0);
-          if (!build_chunk(queue[(qh + lane) & (kBwd2Queue - 1)], 32, first)) ok = false;
-          qh += 32;
-          qn -= 32;
-        }
       }
-      ok = !__any_sync(FULL, !ok);
-      if (!ok) break;
-      // Pool the warps' leftover pairs (< 32 each).
-      __syncwarp();
-      {
-        int base = 0;
-        if (lane == 0 && qn > 0) base = atomicAdd(&left_n[par], qn);
-        base = __shfl_sync(FULL, base, 0);
-        if (lane < qn) left_q[par][base + lane] = queue[(qh + lane) & (kBwd2Queue - 1)];
-      }
-      if (!bsync()) { ok = false; break; }
-      // Every scan chunk is allocated now: the leftover chunks take rows
-      // [T0, T), then zero chunks complete the last stage cs (an extra zero
-      // stage when the scan filled whole stages and nothing is left over).
-      const int T0 = item_rows[par];
-      const int M = left_n[par];
-      const int NL = (M + 31) / 32;
-      const int T = T0 + 32 * NL;
-      int fill;
-      if (T > 0 && !(NL == 0 && T % kTile == 0)) {
-        cs = (int)gs0 + (T - 1) / kTile;
-        fill = T - (cs - (int)gs0) * kTile;
-      } else {
-        cs = (int)gs0 + T / kTile;
-        fill = 0;
-      }
-      cflags = 1 | (T > 0 ? 2 : 0);
-      const int NP = (kTile - fill) / 32;
-      for (int c = bw; c < NL + NP && ok; c += kBwd2Builders / 32) {
-        if (c < NL) {
-          const int n = min(32, M - 32 * c);
-          if (!build_chunk(left_q[par][32 * c + (lane < n ? lane : 0)], n, T0 + 32 * c)) ok = false;
-        } else {
-          const int first = (cs - (int)gs0) * kTile + fill + 32 * (c - NL);
-          if (!build_chunk(make_int4(0, 0, 0, 0), 0, first)) ok = false;
-        }
-      }
-      ok = !__any_sync(FULL, !ok);
-      gs0 = (uint32_t)cs + 1;
     }
     // Copies still in flight complete before the kernel's final barrier.
     tc::cp_async_wait_all();
@@ -1314,8 +1285,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     const int q = warp & 3;
     const int t = q * 32 + lane;   // D row = position in Q
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    uint32_t ac = 0, gs_seen = 0;
-    (void)gs_seen;
+    uint32_t ac = 0;
     for (long long it = blockIdx.x; it < nitems; it += gridDim.x, ++ac) {
       const int buf = ac & 1;
       if (!tc::mbar_wait(acc_full + buf, (ac >> 1) & 1, abort)) break;
@@ -1400,7 +1370,7 @@ int num_sms() {
 }
 
 struct WsLayout {
-  size_t counts, offsets, keyrank, sorted, inv, work, work_count, sbase, scratch, gsh;
+  size_t counts, offsets, keyrank, sorted, inv, work, work_count, sbase, scratch, gsh, f1s;
   size_t fwd_total, total;  // bytes the forward / the backward need
   long long max_work;
 };
@@ -1412,8 +1382,8 @@ WsLayout ws_layout(const TcGeom& g) {
   size_t o = 0;
   const size_t ncells = (size_t)g.B * g.ncell;
   w.max_work = (g.npix + kTile - 1) / kTile + (long long)ncells;
-  w.counts = o; o = align256(o + ncells * 4);
-  w.offsets = o; o = align256(o + ncells * 4);
+  w.counts = o; o = align256(o + ncells * kColBins * 4);
+  w.offsets = o; o = align256(o + (ncells * kColBins + 1) * 4);
   w.keyrank = o; o = align256(o + (size_t)g.npix * 8);
   w.sorted = o; o = align256(o + (size_t)g.npix * 4);
   w.inv = o; o = align256(o + (size_t)g.npix * 4);
@@ -1424,7 +1394,8 @@ WsLayout ws_layout(const TcGeom& g) {
   w.fwd_total = o;
   // the backward's records reuse the forward's output scratch
   w.gsh = w.scratch;
-  w.total = std::max(o, align256(w.gsh + (size_t)g.L * g.npix * g.NG * g.NU * 16));
+  w.f1s = align256(w.gsh + (size_t)g.L * g.npix * g.NG * g.NU * 16);
+  w.total = std::max(o, align256(w.f1s + (size_t)g.npix * g.C * 2));
   return w;
 }
 
@@ -1439,6 +1410,7 @@ struct TcWs {
   int* sbase;
   __half* scratch;
   uint4* gsh;
+  __half* f1s;
 };
 
 TcWs ws_pointers(void* ws, const WsLayout& L) {
@@ -1454,12 +1426,13 @@ TcWs ws_pointers(void* ws, const WsLayout& L) {
   p.sbase = reinterpret_cast<int*>(w + L.sbase);
   p.scratch = reinterpret_cast<__half*>(w + L.scratch);
   p.gsh = reinterpret_cast<uint4*>(w + L.gsh);
+  p.f1s = reinterpret_cast<__half*>(w + L.f1s);
   return p;
 }
 
 // Counting sort of the pixels into anchor cells + the chunk work list.
 bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStream_t s) {
-  if (cudaMemsetAsync(W.counts, 0, sizeof(int) * (size_t)g.B * g.ncell, s) != cudaSuccess)
+  if (cudaMemsetAsync(W.counts, 0, sizeof(int) * (size_t)g.B * g.ncell * kColBins, s) != cudaSuccess)
     return check_launch("memset counts");
   const int threads = 256;
   const int blocks = (int)((g.npix + threads - 1) / threads);
@@ -1610,9 +1583,9 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
 namespace {
 
 size_t bwd1_stage_bytes(const TcGeom& g) { return 16384 + (size_t)g.KC * 8192; }
-size_t bwd2_stage_bytes(const TcGeom& g) { return 32768 + (size_t)g.KC * 16384; }
-// stages, then 512 B of barriers, then the builder warps' pair queues
-constexpr size_t kBwd2Extra = 512 + (size_t)(kBwd2Builders / 32) * kBwd2Queue * 16;
+// A: two 64-position halves of 64 rows; B: KC 64-channel chunks of 64 rows
+size_t bwd2_stage_bytes(const TcGeom& g) { return (size_t)(2 + g.KC) * kB2Rows * 128; }
+constexpr size_t kBwd2Extra = 512;  // barriers after the stages
 size_t bwd2_smem_bytes(int nstage, size_t stage) { return 1024 + (size_t)nstage * stage + kBwd2Extra; }
 
 int pick_stages(size_t stage, size_t extra, int maxst) {
@@ -1629,7 +1602,7 @@ bool bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dila
   if (!eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, &g, &nf)) return false;
   const int nbg = 2;
   const int n1 = pick_stages(bwd1_stage_bytes(g), 256, 4);
-  const int n2 = pick_stages(bwd2_stage_bytes(g), kBwd2Extra, 4);
+  const int n2 = pick_stages(bwd2_stage_bytes(g), kBwd2Extra, 8);
   if (n1 < 2 || n2 < 2) {
     if (why) *why = "tensor-core backward shared-memory budget exceeded";
     return false;
@@ -1699,6 +1672,14 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   }
   TcWs W = ws_pointers(ws, L);
   if (!tc_sort(W, g, co, cdtype, s)) return false;
+  {
+    const int rows_per_block = 8;
+    const long long nb = (g.npix + rows_per_block - 1) / rows_per_block;
+    tc_gather_rows_kernel<<<(unsigned)nb, 32 * rows_per_block, 0, s>>>(
+        static_cast<const __half*>(f1), W.sorted, W.offsets + (size_t)g.B * g.ncell * kColBins, W.f1s, g);
+    count_launch();
+    if (!check_launch("tc_gather_rows")) return false;
+  }
 
   TcBwdParams p1;
   memset(&p1, 0, sizeof(p1));
@@ -1715,6 +1696,20 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) {
       set_error("cuTensorMapEncodeTiled failed for level " + std::to_string(l));
+      return false;
+    }
+  }
+  {
+    cuuint64_t dims[2] = {(cuuint64_t)C, (cuuint64_t)g.npix};
+    cuuint64_t strides[1] = {(cuuint64_t)C * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)kB2Rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = encode(&p1.tmap_f1s, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)W.f1s, dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+      set_error("cuTensorMapEncodeTiled failed for the sorted fmap1 copy");
       return false;
     }
   }

@@ -54,7 +54,7 @@ namespace {
 constexpr int kCellY = 8, kCellX = 16, kTile = 128;
 constexpr int kColBins = kCellX;  // sort bins per cell: the level-0 base column in the cell
 constexpr int kMaxTcLevels = 4;
-constexpr int kBwd1Threads = 64 + 256;  // grad_fmap1: producer, MMA, 2 x 4 builder warps
+constexpr int kBwd1Threads = 64 + 256 + 128;  // grad_fmap1: producer, MMA, 2 x 4 builder warps, 4 epilogue warps
 constexpr int kFwdEG = 3;          // forward epilogue warp groups
 constexpr int kFwdEpiThreads = 64 + 128 * kFwdEG;
 
@@ -809,10 +809,10 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
   uint64_t* bfull = bars;
   uint64_t* afull = bars + NST;
   uint64_t* empty = bars + 2 * NST;
-  uint64_t* acc_full = bars + 3 * NST;
-  uint64_t* acc_empty = acc_full + 1;
-  uint64_t* fin_bar = acc_full + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 3);
+  uint64_t* acc_full = bars + 3 * NST;   // [2]
+  uint64_t* acc_empty = acc_full + 2;    // [2]
+  uint64_t* fin_bar = acc_full + 4;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_full + 5);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -827,14 +827,13 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
       tc::mbar_init(afull + s, kTile);
       tc::mbar_init(empty + s, 1);
     }
-    tc::mbar_init(acc_full, 1);
-    tc::mbar_init(acc_empty, p.nbg * kTile);
+    for (int i = 0; i < 2; ++i) { tc::mbar_init(acc_full + i, 1); tc::mbar_init(acc_empty + i, kTile); }
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
   }
   if (warp == 1) {
-    tc::tmem_alloc(tmem_slot, 256);
+    tc::tmem_alloc(tmem_slot, 512);
     tc::tmem_relinquish();
   }
   tc::tc_fence_before();
@@ -881,7 +880,8 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
       const uint32_t idesc = tc::idesc_f16_f32(128, g.C, false, true);
       bool ok = true;
       for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
-        if (!tc::mbar_wait(acc_empty, (it & 1) ^ 1, abort)) break;
+        const int buf = it & 1;
+        if (!tc::mbar_wait(acc_empty + buf, ((it >> 1) & 1) ^ 1, abort)) break;
         tc::tc_fence_after();
         bool first = true;
         for (int l = 0; l < g.L && ok; ++l) {
@@ -900,41 +900,34 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
             for (int kk = 0; kk < 4; ++kk) {
               const uint64_t ad = tc::smem_desc_sw128(sa + kk * 32, 16, 1024);
               const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, 8192, 1024);
-              tc::mma_f16_ss(tmem, ad, bd, idesc, first ? 0u : 1u);
+              tc::mma_f16_ss(tmem + buf * 256, ad, bd, idesc, first ? 0u : 1u);
               first = false;
             }
             tc::mma_commit(empty + s);
           }
         }
-        if (ok) tc::mma_commit(acc_full);
+        if (ok) tc::mma_commit(acc_full + buf);
       }
       tc::mma_commit(fin_bar);
       tc::mbar_wait(fin_bar, 0, abort);
     }
     __syncwarp();
-  } else {
-    // ---------------- builders + epilogue ----------------
-    // Two groups of 4 warps (each group covers the 128 TMEM lanes): group gb
-    // builds the A tiles of the stages with (stage index & 1) == gb, and
-    // reads columns [gb*C/2, (gb+1)*C/2) of the accumulator at chunk end.
+  } else if (warp < 2 + 4 * p.nbg) {
+    // ---------------- builders ----------------
+    // Groups of 4 warps (one thread per A row = pixel of the chunk): group
+    // gb builds the A tiles of the stages with (stage index % nbg) == gb.
     const int q = warp & 3;
     const int gb = (warp - 2) >> 2;
     const int t = q * 32 + lane;
-    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t gs = 0;
-    int it = 0;
     bool ok = true;
-    for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
+    for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x) {
       const int4 wk = p.work[wi];
       const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
       const bool valid = t < n;
       const int idx = start + t;
-      int gid = 0;
       float cx = 0.f, cy = 0.f;
-      if (valid) {
-        gid = p.sorted[idx];
-        pixel_coords(p, b, gid - b * g.HW, cx, cy);
-      }
+      if (valid) pixel_coords(p, b, p.sorted[idx] - b * g.HW, cx, cy);
       const int ccy = cell / g.ncx, ccx = cell - ccy * g.ncx;
       const int cell_y0 = g.ylo + ccy * kCellY, cell_x0 = g.xlo + ccx * kCellX;
       for (int l = 0; l < g.L && ok; ++l) {
@@ -969,13 +962,25 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
           tc::cp_async_mbar_arrive_noinc(afull + s);
         }
       }
-      if (!ok) break;
-      // epilogue: TMEM row t = this pixel's grad_fmap1 (fp32) -> fp16 row
-      if (!tc::mbar_wait(acc_full, it & 1, abort)) { ok = false; break; }
+    }
+    // Copies still in flight complete before the kernel's final barrier.
+    tc::cp_async_wait_all();
+  } else {
+    // ---------------- epilogue: TMEM row t = pixel t's grad_fmap1 ----------------
+    const int q = warp & 3;
+    const int t = q * 32 + lane;
+    const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
+    int it = 0;
+    for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x, ++it) {
+      const int4 wk = p.work[wi];
+      const int buf = it & 1;
+      const bool valid = t < wk.w;
+      const int gid = valid ? p.sorted[wk.z + t] : 0;
+      if (!tc::mbar_wait(acc_full + buf, (it >> 1) & 1, abort)) break;
       tc::tc_fence_after();
-      for (int c0 = gb * (g.C / p.nbg); c0 < (gb + 1) * (g.C / p.nbg); c0 += 32) {
+      for (int c0 = 0; c0 < g.C; c0 += 32) {
         float v[32];
-        tc::tmem_ld32(lane_addr + c0, v);
+        tc::tmem_ld32(lane_addr + buf * 256 + c0, v);
         tc::tmem_ld_wait();
         if (valid) {
           uint4* dst = reinterpret_cast<uint4*>(p.grad_f1 + (long long)gid * g.C + c0);
@@ -989,7 +994,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
         }
       }
       tc::tc_fence_before();
-      tc::mbar_arrive(acc_empty);
+      tc::mbar_arrive(acc_empty + buf);
     }
   }
 
@@ -997,7 +1002,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
   __syncthreads();
   if (warp == 1) {
     tc::tc_fence_after();
-    tc::tmem_dealloc(tmem, 256);
+    tc::tmem_dealloc(tmem, 512);
   }
   if (threadIdx.x == 0 && abort_flag) atomicExch(&g_tc_status, 1);
 }
@@ -1631,7 +1636,7 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
   const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256;
   auto k1 = tc_bwd1_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k1, smem1)) return false;
-  k1<<<num_sms(), 64 + 128 * p1.nbg, smem1, s>>>(p1);
+  k1<<<num_sms(), 64 + 128 * p1.nbg + 128, smem1, s>>>(p1);
   count_launch();
   if (!check_launch("tc_bwd1")) return false;
   const size_t smem2 = std::max<size_t>(bwd2_smem_bytes(p2.nstage, p2.stage_bytes), 120 * 1024);

@@ -228,12 +228,89 @@ __global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ 
 
 // One CTA: exclusive scan over the cells of the per-cell counts (a cell's
 // count is the sum of its column bins) and of the per-cell chunk counts
+// (work-list offsets). Pass 1 reads every cell's bins (coalesced) into a
+// shared (count, chunks) array; each thread then scans a run of
+// consecutive cells in place and one block scan places the runs; pass 2
+// writes the offsets of every (cell, column) bin into the sorted order
+// (bins in order, so a cell's pixels are sorted by their base column), the
+// work list {b, cell, first sorted index, pixel count <= 128}, and the
+// number of sorted pixels after the last bin.
+constexpr int kScanSmemCells = 24576;  // shared (count, chunks) pairs: 192 KB
+__global__ void __launch_bounds__(1024)
+tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
+               int4* __restrict__ work, int* __restrict__ work_count, int ncell_total,
+               int ncell) {
+  using Scan = cub::BlockScan<int2, 1024>;
+  __shared__ typename Scan::TempStorage tmp;
+  extern __shared__ int2 cs[];
+  auto cell_bins = [&](int i, int* bins) {
+    const int4* src = reinterpret_cast<const int4*>(counts + (long long)i * kColBins);
+#pragma unroll
+    for (int q = 0; q < kColBins / 4; ++q) {
+      const int4 v = src[q];
+      bins[4 * q] = v.x; bins[4 * q + 1] = v.y; bins[4 * q + 2] = v.z; bins[4 * q + 3] = v.w;
+    }
+  };
+  for (int i = threadIdx.x; i < ncell_total; i += blockDim.x) {
+    int bins[kColBins];
+    cell_bins(i, bins);
+    int cnt = 0;
+#pragma unroll
+    for (int q = 0; q < kColBins; ++q) cnt += bins[q];
+    cs[i] = make_int2(cnt, (cnt + kTile - 1) / kTile);
+  }
+  __syncthreads();
+  const int cpt = (ncell_total + 1023) / 1024;
+  const int c0 = min((int)threadIdx.x * cpt, ncell_total), c1 = min(c0 + cpt, ncell_total);
+  int2 run = make_int2(0, 0);
+  for (int i = c0; i < c1; ++i) { run.x += cs[i].x; run.y += cs[i].y; }
+  int2 ex, tot;
+  struct Pair { __device__ int2 operator()(int2 a, int2 b) const { return make_int2(a.x + b.x, a.y + b.y); } };
+  Scan(tmp).ExclusiveScan(run, ex, make_int2(0, 0), Pair(), tot);
+  for (int i = c0; i < c1; ++i) {
+    const int2 v = cs[i];
+    cs[i] = ex;
+    ex.x += v.x;
+    ex.y += v.y;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < ncell_total; i += blockDim.x) {
+    int bins[kColBins];
+    cell_bins(i, bins);
+    const int off = cs[i].x, coff = cs[i].y;
+    int acc = off;
+    int4* dst = reinterpret_cast<int4*>(offsets + (long long)i * kColBins);
+#pragma unroll
+    for (int q = 0; q < kColBins / 4; ++q) {
+      int4 v;
+      v.x = acc; acc += bins[4 * q];
+      v.y = acc; acc += bins[4 * q + 1];
+      v.z = acc; acc += bins[4 * q + 2];
+      v.w = acc; acc += bins[4 * q + 3];
+      dst[q] = v;
+    }
+    const int cnt = acc - off;
+    const int nch = (cnt + kTile - 1) / kTile;
+    const int b = i / ncell;
+    const int cell = i - b * ncell;
+    for (int j = 0; j < nch; ++j)
+      work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
+  }
+  if (threadIdx.x == 0) {
+    *work_count = tot.y;
+    offsets[(long long)ncell_total * kColBins] = tot.x;
+  }
+}
+
+// Fallback for more cells than the shared-memory scan holds.
+// One CTA: exclusive scan over the cells of the per-cell counts (a cell's
+// count is the sum of its column bins) and of the per-cell chunk counts
 // (work-list offsets); writes the offsets of every (cell, column) bin into
 // the sorted order (bins in order, so a cell's pixels are sorted by their
 // base column), a final entry = number of sorted pixels, and the work list:
 // {b, cell, first sorted index, pixel count <= 128}.
 __global__ void __launch_bounds__(1024)
-tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
+tc_scan_big_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
                int4* __restrict__ work, int* __restrict__ work_count, int ncell_total,
                int ncell) {
   using Scan = cub::BlockScan<int2, 1024>;
@@ -885,6 +962,8 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
         tc::tc_fence_after();
         bool first = true;
         for (int l = 0; l < g.L && ok; ++l) {
+          // K positions actually in the group's boxes: whole 16-row MMA steps
+          const int nkk = (g.UWb[l] * g.Rg[l] + 15) / 16;
           for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
             const int s = gs % NST;
             const uint32_t use = gs / NST;
@@ -896,8 +975,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
             tc::tc_fence_after();
             const uint32_t sa = base + s * SB;
             const uint32_t sb = sa + 16384;
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk) {
+            for (int kk = 0; kk < nkk; ++kk) {
               const uint64_t ad = tc::smem_desc_sw128(sa + kk * 32, 16, 1024);
               const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, 8192, 1024);
               tc::mma_f16_ss(tmem + buf * 256, ad, bd, idesc, first ? 0u : 1u);
@@ -937,6 +1015,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
         const int X0 = ((cell_x0 >> l) - RADIUS) & ~7;                // box column 0
         const int cu = (((bxl - RADIUS) & ~7) - X0) >> 3;             // box unit of record unit 0
         const int UPR = g.UWb[l] >> 3, Rg = g.Rg[l];
+        const int nunit = 2 * ((g.UWb[l] * Rg + 15) / 16);  // A units the MMA reads
         const uint4* rec = p.gsh + ((long long)l * g.npix + idx) * (NG * NU);
         for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
           if ((int)(gs % (uint32_t)p.nbg) != gb) continue;
@@ -949,6 +1028,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
           int br = 0, uc = 0;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
+            if (k >= nunit) break;  // past the MMA's K steps: never read
             const int jj = gi * Rg + br - ry;
             const int u = uc - cu;
             uint8_t* dst = arow + ((k ^ (t & 7)) << 4);
@@ -1447,8 +1527,16 @@ bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStr
     tc_hist_kernel<__half><<<blocks, threads, 0, s>>>((const __half*)co, W.counts, W.keyrank, g);
   count_launch();
   if (!check_launch("tc_hist")) return false;
-  tc_scan_kernel<<<1, 1024, 0, s>>>(W.counts, W.offsets, W.work, W.work_count, g.B * g.ncell,
-                                    g.ncell);
+  const int ncells = g.B * g.ncell;
+  if (ncells <= kScanSmemCells) {
+    const size_t smem = (size_t)ncells * sizeof(int2);
+    if (!ensure_smem_attr((const void*)tc_scan_kernel, smem)) return false;
+    tc_scan_kernel<<<1, 1024, smem, s>>>(W.counts, W.offsets, W.work, W.work_count, ncells,
+                                         g.ncell);
+  } else {
+    tc_scan_big_kernel<<<1, 1024, 0, s>>>(W.counts, W.offsets, W.work, W.work_count, ncells,
+                                          g.ncell);
+  }
   count_launch();
   if (!check_launch("tc_scan")) return false;
   tc_scatter_kernel<<<blocks, threads, 0, s>>>(W.keyrank, W.offsets, W.sorted, W.inv, g);

@@ -72,6 +72,24 @@ def _peaks():
     return 6650.0, "fallback"
 
 
+def max_over_ranks(value, dist, device):
+    """The job's elapsed time: the slowest rank's (no-op on one process)."""
+    if dist is None:
+        return float(value)
+    t = torch.tensor([float(value)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(value, dist, device):
+    """Whole-job total of a per-rank count (no-op on one process)."""
+    if dist is None:
+        return value
+    t = torch.tensor([float(value)], device=device, dtype=torch.float64)
+    dist.all_reduce(t)
+    return t.item()
+
+
 def lookups_per_call(cfg):
     return cfg["B"] * cfg["H"] * cfg["W"] * cfg["L"] * (2 * cfg["r"] + 1) ** 2
 
@@ -187,9 +205,10 @@ def make_inputs(cfg, rank, device):
     if cfg["backward"]:
         grads = [torch.randn(b, cfg["L"] * rd * rd, h, w, generator=g).to(dt)
                  for _ in range(cfg["iters"])]
+    pin = (lambda t: t.pin_memory()) if torch.cuda.is_available() else (lambda t: t)
     host = dict(
-        f1=f1.to(dt).pin_memory(), f2=f2.to(dt).pin_memory(),
-        coords=[co.to(dt).pin_memory() for co in coords],
+        f1=pin(f1.to(dt)), f2=pin(f2.to(dt)),
+        coords=[pin(co.to(dt)) for co in coords],
     )
     dev = dict(
         f1=host["f1"].to(device), f2=host["f2"].to(device),
@@ -308,6 +327,7 @@ def main(argv=None):
 
         import torch.distributed as dist
 
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=device)
     from localcorr_b200 import _lib, ops
@@ -339,13 +359,8 @@ def main(argv=None):
     launches = int(lib.localCorrB200LaunchCount(1))
     ops.set_launch_timer(None)
     clocks = sampler.stop() if sampler else None
-    if dist is not None:
-        t = torch.tensor([elapsed], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed = float(t.item())
-        n = torch.tensor([launches], device=device, dtype=torch.float64)
-        dist.all_reduce(n)
-        launches = int(n.item())
+    elapsed = max_over_ranks(elapsed, dist, device)
+    launches = int(sum_over_ranks(launches, dist, device))
 
     # per-kernel durations from the live events
     per = {}
@@ -367,10 +382,7 @@ def main(argv=None):
     barrier()
     e2e_elapsed = timed_loop(e2e_step, args.steps, device)
     barrier()
-    if dist is not None:
-        t = torch.tensor([e2e_elapsed], device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_elapsed = float(t.item())
+    e2e_elapsed = max_over_ranks(e2e_elapsed, dist, device)
 
     lookups_step = lookups_per_call(cfg) * cfg["iters"]
     value = lookups_step * args.steps * world / elapsed / 1e9

@@ -98,14 +98,20 @@ LCB200_API bool launchLocalCorrB200PyramidForward(
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* Backward of launchLocalCorrB200PyramidForward (gradient of the scaled
- * output). fmap1_grad (dtype) is overwritten. fmap2_grad_f32 (float32,
- * fmap2_packed's element count) is accumulated into when accumulate is true
- * and overwritten otherwise. */
+ * output). accumulate is a set of flags:
+ *   LCB200_ACC_FMAP2: add into fmap2_grad_f32 (float32, fmap2_packed's element
+ *                     count) instead of overwriting it;
+ *   LCB200_ACC_FMAP1: add into fmap1_grad (dtype) instead of overwriting it.
+ * (1 = LCB200_ACC_FMAP2 keeps the meaning of a plain `true`.) Accumulating
+ * both lets the lookups of one pair of maps share one pair of gradient
+ * buffers instead of summing per-lookup gradients afterwards. */
+#define LCB200_ACC_FMAP2 1
+#define LCB200_ACC_FMAP1 2
 LCB200_API bool launchLocalCorrB200PyramidBackward(
     const void* fmap1, const void* fmap2_packed, const void* coords,
     const void* corr_grad, void* fmap1_grad, float* fmap2_grad_f32,
     int B, int H1, int W1, int C, int radius, int levels, int dilation,
-    int dtype, int coords_dtype, bool ymajor, float scale, bool accumulate, int engine,
+    int dtype, int coords_dtype, bool ymajor, float scale, int accumulate, int engine,
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
 /* ---- Allocation-free forward (no counterpart in the reference) -------------

@@ -19,6 +19,8 @@ LIB_PATH = Path(__file__).resolve().parent / "liblocalcorr_b200.so"
 
 F32 = 0
 F16 = 1
+ACC_FMAP2 = 1  # backward: add into the float32 fmap2 gradient
+ACC_FMAP1 = 2  # backward: add into the fmap1 gradient
 ENGINE_AUTO = 0
 ENGINE_SIMT = 1
 ENGINE_TC = 2
@@ -50,7 +52,7 @@ PROTOTYPES = {
         _c_bool,
         [_c_void_p] * 6
         + [_c_int] * 7
-        + [_c_int, _c_int, _c_bool, _c_float, _c_bool, _c_int, _c_void_p, _c_size_t, _c_void_p],
+        + [_c_int, _c_int, _c_bool, _c_float, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p],
     ),
     "launchLocalCorrB200PyramidForwardNoAlloc": (
         _c_bool,

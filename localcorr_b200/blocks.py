@@ -232,6 +232,16 @@ class LocalCorrCudaPyramidBlock:
                 f"{fmap1.dtype} and {fmap2.dtype}.")
         self.fmap1 = ops.NchwToNhwc.apply(fmap1)
         self.fmap2_packed = ops.PyramidBuild.apply(fmap2, self.num_levels)
+        # Lookups read detached copies of the prepared maps and send their
+        # gradients through one token into shared accumulators (see
+        # ops.LookupGrads); the attributes above stay differentiable for
+        # callers that use them directly.
+        self._grads = None
+        self._token = None
+        if torch.is_grad_enabled() and (fmap1.requires_grad or fmap2.requires_grad):
+            self._grads = ops.LookupGrads(self.fmap1.detach(), self.fmap2_packed.detach(),
+                                          fmap2.shape, self.num_levels)
+            self._token = ops.LookupGradSink.apply(fmap1, fmap2, self._grads)
         b, c, h, w = fmap2.shape
         self.fmap2_pyramid = []
         off = 0
@@ -254,9 +264,13 @@ class LocalCorrCudaPyramidBlock:
         _lib.require_library()
         if coords.dtype not in (torch.float32, torch.float16):
             raise RuntimeError(f"coords must be float32 or float16, got {coords.dtype}")
-        corr = ops.ScaledPyramidCorr.apply(self.fmap1, self.fmap2_packed, coords, self.radius,
-                                           self.num_levels, 1, False,
-                                           1.0 / math.sqrt(self.dim))
+        scale = 1.0 / math.sqrt(self.dim)
+        if self._token is not None and torch.is_grad_enabled():
+            corr = ops.PyramidLookup.apply(self._token, coords, self._grads, self.radius,
+                                           self.num_levels, scale)
+        else:
+            corr = ops.ScaledPyramidCorr.apply(self.fmap1, self.fmap2_packed, coords,
+                                               self.radius, self.num_levels, 1, False, scale)
         return corr.reshape(b, -1, h, w)
 
     def _export(self, coords):

@@ -13,14 +13,14 @@ namespace lcb200 {
 bool simt_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
                   int, int, int, bool, float, cudaStream_t);
 bool simt_backward(const void*, const void*, const void*, const void*, void*, float*, int,
-                   int, int, int, int, int, int, int, int, bool, float, cudaStream_t);
+                   int, int, int, int, int, int, int, int, bool, float, bool, cudaStream_t);
 bool tc_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
                  int dtype, std::string* why);
 size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels, bool backward);
 bool tc_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
                 int, bool, float, void*, size_t, cudaStream_t);
 bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int, int,
-                 int, int, int, int, int, bool, float, void*, size_t, cudaStream_t);
+                 int, int, int, int, int, bool, float, bool, void*, size_t, cudaStream_t);
 bool tc_bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
                      int dtype, std::string* why);
 int tc_device_status(bool reset);
@@ -223,7 +223,7 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
 bool pyramid_backward(const void* f1, const void* f2, const void* co, const void* gout,
                       void* f1g, float* f2g, int B, int H1, int W1, int C, int radius,
                       int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
-                      bool accumulate, int engine, void* ws, size_t ws_bytes, bool lib_ws,
+                      int accumulate, int engine, void* ws, size_t ws_bytes, bool lib_ws,
                       cudaStream_t s) {
   clear_error();
   bool empty = false;
@@ -233,7 +233,8 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
     set_error("coords dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
     return false;
   }
-  if (!accumulate) {
+  const bool acc1 = (accumulate & LCB200_ACC_FMAP1) != 0;
+  if (!(accumulate & LCB200_ACC_FMAP2)) {
     const PyrGeom g = make_geom(H1, W1, C, levels);
     if (cudaMemsetAsync(f2g, 0, sizeof(float) * (size_t)B * g.batch_elems, s) != cudaSuccess)
       return check_launch("memset fmap2_grad");
@@ -251,11 +252,11 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
       return false;
     }
     return tc_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, radius, levels, cdtype, ymajor,
-                       scale, ws, ws_bytes, s);
+                       scale, acc1, ws, ws_bytes, s);
   }
   if (!ok) return false;
   return simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, radius, levels, dil, dtype,
-                       cdtype, ymajor, scale, s);
+                       cdtype, ymajor, scale, acc1, s);
 }
 
 bool validate_layout(int B, int C, int H, int W, int dtype) {
@@ -294,7 +295,7 @@ bool launchLocalCorrCudaPyramidBackward(const void* fmap1, const void* fmap2_pac
                                         bool isHalf, bool ymajor, cudaStream_t stream) {
   return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad, B, H1,
                           W1, C, radius, levels, dilation, isHalf ? LCB200_F16 : LCB200_F32,
-                          isHalf ? LCB200_F16 : LCB200_F32, ymajor, 1.0f, true,
+                          isHalf ? LCB200_F16 : LCB200_F32, ymajor, 1.0f, LCB200_ACC_FMAP2,
                           LCB200_ENGINE_AUTO, nullptr, 0, true, stream);
 }
 
@@ -328,7 +329,7 @@ bool launchLocalCorrB200PyramidBackward(const void* fmap1, const void* fmap2_pac
                                         void* fmap1_grad, float* fmap2_grad_f32, int B, int H1,
                                         int W1, int C, int radius, int levels, int dilation,
                                         int dtype, int coords_dtype, bool ymajor, float scale,
-                                        bool accumulate, int engine, void* workspace,
+                                        int accumulate, int engine, void* workspace,
                                         size_t workspace_bytes, cudaStream_t stream) {
   return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad_f32, B,
                           H1, W1, C, radius, levels, dilation, dtype, coords_dtype, ymajor,

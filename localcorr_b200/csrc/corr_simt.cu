@@ -154,7 +154,7 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
                      const TC* __restrict__ coords, const T* __restrict__ corr_grad,
                      T* __restrict__ fmap1_grad, float* __restrict__ fmap2_grad,
                      int H1, int W1, int C, int r, int dil, bool ymajor,
-                     float scale, PyrGeom g) {
+                     float scale, bool acc1, PyrGeom g) {
   constexpr int PG = kWarps * PPW;
   extern __shared__ float smem[];
   const int RD = 2 * r + 1;
@@ -254,7 +254,10 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
   for (int i = threadIdx.x; i < PG * C; i += kThreads) {
     const int q = i / C;
     const int c = i - q * C;
-    if (q < npix) stf(fmap1_grad + ((long long)b * HW + p0 + q) * C + c, f1g[i]);
+    if (q < npix) {
+      T* dst = fmap1_grad + ((long long)b * HW + p0 + q) * C + c;
+      stf(dst, acc1 ? ldf(dst) + f1g[i] : f1g[i]);
+    }
   }
 }
 
@@ -282,13 +285,14 @@ bool launch_fwd(const void* f1, const void* f2, const void* co, void* out, int B
 template <typename T, typename TC, int PPW>
 bool launch_bwd(const void* f1, const void* f2, const void* co, const void* gout,
                 void* f1g, float* f2g, int B, int H1, int W1, int C, int r, int dil,
-                bool ymajor, float scale, const PyrGeom& g, size_t smem, cudaStream_t s) {
+                bool ymajor, float scale, bool acc1, const PyrGeom& g, size_t smem,
+                cudaStream_t s) {
   auto k = corr_bwd_simt_kernel<T, TC, PPW>;
   if (!ensure_smem_attr((const void*)k, smem)) return false;
   const int PG = kWarps * PPW;
   dim3 grid((H1 * W1 + PG - 1) / PG, B);
   k<<<grid, kThreads, smem, s>>>((const T*)f1, (const T*)f2, (const TC*)co, (const T*)gout,
-                                 (T*)f1g, f2g, H1, W1, C, r, dil, ymajor, scale, g);
+                                 (T*)f1g, f2g, H1, W1, C, r, dil, ymajor, scale, acc1, g);
   count_launch();
   return check_launch("corr_bwd_simt");
 }
@@ -331,7 +335,7 @@ bool simt_forward(const void* f1, const void* f2, const void* co, void* out, int
 bool simt_backward(const void* f1, const void* f2, const void* co, const void* gout,
                    void* f1g, float* f2g, int B, int H1, int W1, int C, int r,
                    int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
-                   cudaStream_t s) {
+                   bool acc1, cudaStream_t s) {
   const PyrGeom g = make_geom(H1, W1, C, levels);
   const int RD = 2 * r + 1;
   const int NX = (dil == 1) ? RD + 1 : 2 * RD;
@@ -347,9 +351,9 @@ bool simt_backward(const void* f1, const void* f2, const void* co, const void* g
   }
 #define LCB_BWD(T, TC)                                                                        \
   return ppw == 4 ? launch_bwd<T, TC, 4>(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, r, dil,    \
-                                         ymajor, scale, g, smem, s)                            \
+                                         ymajor, scale, acc1, g, smem, s)                      \
                   : launch_bwd<T, TC, 1>(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, r, dil,    \
-                                         ymajor, scale, g, smem, s);
+                                         ymajor, scale, acc1, g, smem, s);
   if (dtype == LCB200_F32) {
     if (cdtype == LCB200_F32) { LCB_BWD(float, float) }
     LCB_BWD(float, __half)

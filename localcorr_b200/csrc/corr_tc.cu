@@ -706,7 +706,7 @@ __global__ void __launch_bounds__(128)
 tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
                int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
                int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale, int ymajor,
-               int vec_ok, TcGeom g) {
+               int vec_ok, int acc_f1, TcGeom g) {
   using S = GintShape<RADIUS>;
   constexpr int RD = S::RD, NG = S::NG, NU = S::NU, RC = S::RC, SU = S::SU;
   constexpr unsigned FULL = 0xffffffffu;
@@ -740,7 +740,7 @@ tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ co
     const long long gid = (long long)b * g.HW + pix;
     idx = inv[gid];
     if (idx < 0) {
-      if (l == 0) {
+      if (l == 0 && !acc_f1) {
         uint4* row = reinterpret_cast<uint4*>(grad_f1 + gid * g.C);
         for (int i = 0; i < g.C / 8; ++i) row[i] = make_uint4(0, 0, 0, 0);
       }
@@ -847,7 +847,8 @@ struct alignas(64) TcBwdParams {
   int nstage;
   uint32_t stage_bytes;
   long long nitems;
-  int nbg;  // grad_fmap1 builder groups (1 or 2)
+  int nbg;     // grad_fmap1 builder groups (1 or 2)
+  int acc_f1;  // add grad_fmap1 into the existing rows instead of overwriting them
   TcGeom g;
 };
 
@@ -1066,6 +1067,18 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
           uint4* dst = reinterpret_cast<uint4*>(p.grad_f1 + (long long)gid * g.C + c0);
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
+            if (p.acc_f1) {
+              // add the existing row (in its float16 storage type, as a sum
+              // of per-lookup float16 gradients would be)
+              const uint4 old = dst[i];
+              const __half2* o2 = reinterpret_cast<const __half2*>(&old);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float2 of = __half22float2(o2[e]);
+                v[8 * i + 2 * e] += of.x;
+                v[8 * i + 2 * e + 1] += of.y;
+              }
+            }
             __align__(16) __half2 h2[4];
 #pragma unroll
             for (int e = 0; e < 4; ++e) h2[e] = __floats2half2_rn(v[8 * i + 2 * e], v[8 * i + 2 * e + 1]);
@@ -1718,7 +1731,8 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
   // aligned base
   const int vec_ok = (g.HW % 8 == 0) && (reinterpret_cast<uintptr_t>(corr_grad) % 16 == 0);
   k0<<<ug, 128, smem0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gsh,
-                            const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, vec_ok, g);
+                            const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, vec_ok,
+                            p1.acc_f1, g);
   count_launch();
   if (!check_launch("tc_gint")) return false;
   const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256;
@@ -1745,7 +1759,8 @@ bool tc_bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int d
 
 bool tc_backward(const void* f1, const void* f2, const void* co, const void* gout, void* f1g,
                  float* f2g, int B, int H1, int W1, int C, int radius, int levels, int cdtype,
-                 bool ymajor, float scale, void* ws, size_t ws_bytes, cudaStream_t s) {
+                 bool ymajor, float scale, bool acc_f1, void* ws, size_t ws_bytes,
+                 cudaStream_t s) {
   TcGeom g;
   int n1 = 0, n2 = 0;
   std::string why;
@@ -1818,6 +1833,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.fmap1 = static_cast<const __half*>(f1);
   p1.grad_f1 = static_cast<__half*>(f1g);
   p1.grad_f2 = f2g;
+  p1.acc_f1 = acc_f1 ? 1 : 0;
   p1.g = g;
   p1.nitems = (long long)B * g.items_before[levels];
   TcBwdParams p2 = p1;

@@ -167,8 +167,13 @@ def pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation=1
 
 
 def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels,
-                          dilation=1, ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO):
-    """Returns (grad_fmap1 [B,H,W,C] dtype, grad_fmap2_packed float32)."""
+                          dilation=1, ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO,
+                          out=None, accumulate=0):
+    """Returns (grad_fmap1 [B,H,W,C] dtype, grad_fmap2_packed float32).
+
+    With ``out=(g1, g2)`` the gradients go into those buffers; ``accumulate``
+    (flags ``_lib.ACC_FMAP1`` / ``_lib.ACC_FMAP2``) adds into them instead of
+    overwriting."""
     lib = _lib.require_library()
     b, h, w, c = fmap1.shape
     dt = _dtype_code(fmap1)
@@ -176,15 +181,18 @@ def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels
     corr_grad = corr_grad.contiguous()
     if corr_grad.dtype != fmap1.dtype:
         corr_grad = corr_grad.to(fmap1.dtype)
-    g1 = torch.empty_like(fmap1)
-    g2 = torch.empty(fmap2_packed.shape, dtype=torch.float32, device=fmap1.device)
+    if out is not None:
+        g1, g2 = out
+    else:
+        g1 = torch.empty_like(fmap1)
+        g2 = torch.empty(fmap2_packed.shape, dtype=torch.float32, device=fmap1.device)
     nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine)
     ws, nws = _workspace(fmap1, nbytes)
     with torch.cuda.device(fmap1.device):
         ok = _timed("pyramid_bwd", lambda: lib.launchLocalCorrB200PyramidBackward(
             fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr_grad.data_ptr(),
             g1.data_ptr(), g2.data_ptr(), b, h, w, c, radius, levels, dilation, dt, cdt,
-            bool(ymajor), float(scale), False, engine,
+            bool(ymajor), float(scale), int(accumulate), engine,
             ws.data_ptr() if ws is not None else None, nws, _stream(fmap1)))
     _lib.check(ok, "pyramid correlation backward", lib)
     return g1, g2
@@ -282,6 +290,89 @@ class ScaledPyramidCorr(torch.autograd.Function):
         # returns (blocks.py:534-537).
         gc = torch.zeros_like(coords) if ctx.needs_input_grad[2] else None
         return g1, g2, gc, None, None, None, None, None
+
+
+class LookupGrads:
+    """Gradient accumulators shared by the lookups of one pyramid block.
+
+    Every lookup's backward adds its fmap1 gradient (NHWC, map dtype) and its
+    fmap2 gradient (packed, float32) into these buffers through the C ABI's
+    accumulate flags; the first lookup of a backward pass overwrites them.
+    ``LookupGradSink``'s backward, which autograd runs once after all of
+    them, turns the sums into the NCHW gradients and resets the state. This
+    replaces one gradient allocation, one float16 cast and one autograd
+    addition per lookup and map by a single pass at the end.
+    """
+
+    def __init__(self, fmap1_nhwc, fmap2_packed, fmap2_shape, levels):
+        self.fmap1 = fmap1_nhwc
+        self.fmap2_packed = fmap2_packed
+        self.fmap2_shape = tuple(fmap2_shape)
+        self.levels = int(levels)
+        self.g1 = None
+        self.g2 = None
+
+    def buffers(self):
+        """(g1, g2, flags) for the next lookup's backward."""
+        if self.g1 is None:
+            self.g1 = torch.empty_like(self.fmap1)
+            self.g2 = torch.empty(self.fmap2_packed.shape, dtype=torch.float32,
+                                  device=self.fmap1.device)
+            return self.g1, self.g2, 0
+        return self.g1, self.g2, _lib.ACC_FMAP1 | _lib.ACC_FMAP2
+
+
+class LookupGradSink(torch.autograd.Function):
+    """Joins a block's lookups to its NCHW feature maps through one token.
+
+    The token (a 0-dim tensor) is an input of every lookup; its gradient is
+    zero, and this backward runs after every lookup's backward (autograd
+    waits for all of the token's gradients), returning the accumulated NCHW
+    gradients of fmap1 and fmap2.
+    """
+
+    @staticmethod
+    def forward(ctx, fmap1, fmap2, state):
+        ctx.state = state
+        ctx.dtype = fmap2.dtype
+        return fmap1.new_zeros(())
+
+    @staticmethod
+    def backward(ctx, _):
+        st = ctx.state
+        g1 = g2 = None
+        if st.g1 is not None:
+            if ctx.needs_input_grad[0]:
+                g1 = nhwc_to_nchw(st.g1)
+            if ctx.needs_input_grad[1]:
+                g2 = pyramid_build_backward(st.g2, st.fmap2_shape, st.levels, ctx.dtype)
+        st.g1 = st.g2 = None
+        return g1, g2, None
+
+
+class PyramidLookup(torch.autograd.Function):
+    """One lookup of a pyramid block whose gradients go to ``LookupGrads``."""
+
+    @staticmethod
+    def forward(ctx, token, coords, state, radius, levels, scale):
+        coords = coords.contiguous()
+        corr = pyramid_corr_forward(state.fmap1, state.fmap2_packed, coords, radius, levels,
+                                    1, False, scale)
+        ctx.save_for_backward(coords)
+        ctx.state = state
+        ctx.params = (int(radius), int(levels), float(scale))
+        return corr
+
+    @staticmethod
+    def backward(ctx, corr_grad):
+        (coords,) = ctx.saved_tensors
+        st = ctx.state
+        radius, levels, scale = ctx.params
+        g1, g2, flags = st.buffers()
+        pyramid_corr_backward(st.fmap1, st.fmap2_packed, coords, corr_grad, radius, levels,
+                              1, False, scale, out=(g1, g2), accumulate=flags)
+        gc = torch.zeros_like(coords) if ctx.needs_input_grad[1] else None
+        return corr_grad.new_zeros(()), gc, None, None, None, None
 
 
 class SpatialCorr(torch.autograd.Function):

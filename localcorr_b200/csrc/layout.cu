@@ -30,8 +30,39 @@ __global__ void transpose_kernel(const T* __restrict__ in, T* __restrict__ out,
   }
 }
 
+// float16 with even R and Ccols: 64x64 tiles, each thread moving half2
+// pairs on both sides (4-byte accesses, 128 bytes per warp access).
+__global__ void transpose_h2_kernel(const __half* __restrict__ in, __half* __restrict__ out,
+                                    int R, int Ccols) {
+  __shared__ __half tile[64][66];
+  const long long bo = (long long)blockIdx.z * R * Ccols;
+  const int c0 = blockIdx.x * 64, r0 = blockIdx.y * 64;
+  const int tx = threadIdx.x, ty = threadIdx.y;  // 32 x 8
+  for (int i = ty; i < 64; i += 8) {
+    const int rr = r0 + i, cc = c0 + 2 * tx;
+    __half2 v = __floats2half2_rn(0.f, 0.f);
+    if (rr < R && cc < Ccols) v = *reinterpret_cast<const __half2*>(in + bo + (long long)rr * Ccols + cc);
+    tile[i][2 * tx] = __low2half(v);
+    tile[i][2 * tx + 1] = __high2half(v);
+  }
+  __syncthreads();
+  for (int i = ty; i < 64; i += 8) {
+    const int cc = c0 + i, rr = r0 + 2 * tx;
+    if (cc < Ccols && rr < R)
+      *reinterpret_cast<__half2*>(out + bo + (long long)cc * R + rr) =
+          __halves2half2(tile[2 * tx][i], tile[2 * tx + 1][i]);
+  }
+}
+
 template <typename T>
 bool launch_transpose(const void* in, void* out, int B, int R, int Ccols, cudaStream_t s) {
+  if (std::is_same<T, __half>::value && R % 2 == 0 && Ccols % 2 == 0 &&
+      ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 3) == 0) {
+    dim3 grid((Ccols + 63) / 64, (R + 63) / 64, B);
+    transpose_h2_kernel<<<grid, dim3(32, 8), 0, s>>>((const __half*)in, (__half*)out, R, Ccols);
+    count_launch();
+    return check_launch("transpose");
+  }
   dim3 grid((Ccols + 31) / 32, (R + 31) / 32, B);
   transpose_kernel<T><<<grid, dim3(32, 8), 0, s>>>((const T*)in, (T*)out, R, Ccols);
   count_launch();
@@ -192,6 +223,86 @@ pyramid_grad_kernel(const G* __restrict__ gp, T* __restrict__ out, int C, int H,
   }
 }
 
+// Gradient of the pyramid build for float32 level gradients and a float16
+// NCHW result (the path the block's autograd takes): CTA = 16x32 level-0
+// tile x 32 channels. The coarse levels collapse first into the tile's
+// level-1 footprint, c1 = g1 + (g2 + g3/4)/4 (16 KB of shared memory, 16-byte
+// channel-quad loads), then out = g0 + c1/4 per level-0 pixel, staged as
+// [channel][pixel] float16 and written along x in 8-byte pieces.
+// Needs C % 32 == 0, W % 4 == 0 and at most 4 levels.
+constexpr int kGY = 16, kGX = 32, kGC = 32;
+constexpr int kGS = kGY * kGX + 4;  // staging row stride in halves (8-byte aligned rows)
+constexpr size_t kGradSmem = (size_t)(kGY / 2) * (kGX / 2) * kGC * 4 + (size_t)kGC * kGS * 2;
+
+__global__ void __launch_bounds__(256)
+pyramid_grad_f32_kernel(const float* __restrict__ gp, __half* __restrict__ out, int C, int H,
+                        int W, PyrGeom g) {
+  extern __shared__ __align__(16) uint8_t gsm[];
+  float4* c1 = reinterpret_cast<float4*>(gsm);  // [(kGY/2)*(kGX/2)][kGC/4]
+  __half* st = reinterpret_cast<__half*>(gsm + (size_t)(kGY / 2) * (kGX / 2) * kGC * 4);
+  const int b = blockIdx.z;
+  const int c0 = blockIdx.y * kGC;
+  const int tiles_x = (W + kGX - 1) / kGX;
+  const int ty0 = (blockIdx.x / tiles_x) * kGY;
+  const int tx0 = (blockIdx.x % tiles_x) * kGX;
+  const float* gb = gp + (long long)b * g.batch_elems + c0;
+  auto lvl = [&](int l, int y, int x, int cq) -> float4 {  // level-l quad, zero off the level
+    if (l >= g.levels || y >= g.h[l] || x >= g.w[l]) return make_float4(0.f, 0.f, 0.f, 0.f);
+    return *reinterpret_cast<const float4*>(gb + g.off[l] + ((long long)y * g.w[l] + x) * C +
+                                            4 * cq);
+  };
+  const int tid = threadIdx.x;
+  if (g.levels > 1) {
+    for (int i = tid; i < (kGY / 2) * (kGX / 2) * (kGC / 4); i += 256) {
+      const int cq = i % (kGC / 4), p1 = i / (kGC / 4);
+      const int y1 = ty0 / 2 + p1 / (kGX / 2), x1 = tx0 / 2 + p1 % (kGX / 2);
+      float4 v = lvl(1, y1, x1, cq);
+      if (g.levels > 2) {
+        float4 v2 = lvl(2, y1 >> 1, x1 >> 1, cq);
+        if (g.levels > 3) {
+          const float4 v3 = lvl(3, y1 >> 2, x1 >> 2, cq);
+          v2.x += 0.25f * v3.x; v2.y += 0.25f * v3.y; v2.z += 0.25f * v3.z; v2.w += 0.25f * v3.w;
+        }
+        v.x += 0.25f * v2.x; v.y += 0.25f * v2.y; v.z += 0.25f * v2.z; v.w += 0.25f * v2.w;
+      }
+      c1[p1 * (kGC / 4) + cq] = v;
+    }
+    __syncthreads();
+  }
+  for (int i = tid; i < kGY * kGX * (kGC / 4); i += 256) {
+    const int cq = i % (kGC / 4), p0 = i / (kGC / 4);
+    const int y = p0 / kGX, x = p0 % kGX;
+    const int gy = ty0 + y, gx = tx0 + x;
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (gy < H && gx < W) {
+      v = *reinterpret_cast<const float4*>(gb + ((long long)gy * W + gx) * C + 4 * cq);
+      if (g.levels > 1) {
+        const float4 u = c1[((y >> 1) * (kGX / 2) + (x >> 1)) * (kGC / 4) + cq];
+        v.x += 0.25f * u.x; v.y += 0.25f * u.y; v.z += 0.25f * u.z; v.w += 0.25f * u.w;
+      }
+    }
+    __half* d = st + (4 * cq) * kGS + p0;
+    d[0] = __float2half_rn(v.x);
+    d[kGS] = __float2half_rn(v.y);
+    d[2 * kGS] = __float2half_rn(v.z);
+    d[3 * kGS] = __float2half_rn(v.w);
+  }
+  __syncthreads();
+  for (int i = tid; i < kGC * kGY * (kGX / 4); i += 256) {
+    const int xq = i % (kGX / 4), rest = i / (kGX / 4);
+    const int y = rest % kGY, c = rest / kGY;
+    const int gy = ty0 + y, gx = tx0 + 4 * xq;
+    if (gy >= H || gx >= W) continue;
+    const __half* src = st + c * kGS + y * kGX + 4 * xq;
+    __half* dst = out + (((long long)b * C + c0 + c) * H + gy) * W + gx;
+    if (gx + 3 < W) {
+      *reinterpret_cast<uint2*>(dst) = *reinterpret_cast<const uint2*>(src);
+    } else {
+      for (int e = 0; gx + e < W; ++e) dst[e] = src[e];
+    }
+  }
+}
+
 template <typename T>
 bool launch_build(const void* in, void* packed, int B, int C, int H, int W, int levels,
                   cudaStream_t s) {
@@ -217,6 +328,17 @@ template <typename T, typename G>
 bool launch_build_grad(const void* gp, void* out, int B, int C, int H, int W, int levels,
                        cudaStream_t s) {
   const PyrGeom g = make_geom(H, W, C, levels);
+  if (std::is_same<T, __half>::value && std::is_same<G, float>::value && C % kGC == 0 &&
+      W % 4 == 0 && levels <= 4 && (reinterpret_cast<uintptr_t>(gp) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(out) & 7) == 0) {
+    if (!ensure_smem_attr((const void*)pyramid_grad_f32_kernel, kGradSmem)) return false;
+    const int tiles = ((H + kGY - 1) / kGY) * ((W + kGX - 1) / kGX);
+    dim3 grid(tiles, C / kGC, B);
+    pyramid_grad_f32_kernel<<<grid, 256, kGradSmem, s>>>((const float*)gp, (__half*)out, C, H,
+                                                         W, g);
+    count_launch();
+    return check_launch("pyramid_build_grad");
+  }
   constexpr int CC = 32;
   const int tiles = ((H + kTY - 1) / kTY) * ((W + kTX - 1) / kTX);
   dim3 grid(tiles, (C + CC - 1) / CC, B);

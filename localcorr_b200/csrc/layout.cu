@@ -156,6 +156,79 @@ pyramid_build_kernel(const T* __restrict__ in, T* __restrict__ packed, int C, in
 }
 
 // Levels >= 4: pool level l-1 of the packed buffer into level l (NHWC).
+// float16 pyramid build with half2 accesses: CTA = 8x32 level-0 tile x 64
+// channels, levels kept in shared memory as float16 [y][x][64+2] (the stored
+// values are the dtype-rounded level values that the next level pools). The
+// NCHW tile is read as x pairs; every NHWC row of 64 channels (128 bytes) is
+// written by one warp as channel pairs. Needs C % 64 == 0 and W even.
+constexpr int kHC = 64, kHP = kHC + 2;
+__global__ void __launch_bounds__(256)
+pyramid_build_h_kernel(const __half* __restrict__ in, __half* __restrict__ packed, int C, int H,
+                       int W, PyrGeom g, int nlev) {
+  __shared__ __align__(16) __half s0[kTY * kTX * kHP];
+  __shared__ __align__(16) __half s1[(kTY / 2) * (kTX / 2) * kHP];
+  const int b = blockIdx.z;
+  const int c0 = blockIdx.y * kHC;
+  const int tiles_x = (W + kTX - 1) / kTX;
+  const int ty0 = (blockIdx.x / tiles_x) * kTY;
+  const int tx0 = (blockIdx.x % tiles_x) * kTX;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  // NCHW tile: item = (c, y, x pair)
+  for (int i = tid; i < kHC * kTY * (kTX / 2); i += 256) {
+    const int xp = i % (kTX / 2), rest = i / (kTX / 2);
+    const int y = rest % kTY, c = rest / kTY;
+    const int gy = ty0 + y, gx = tx0 + 2 * xp;
+    __half2 v = __floats2half2_rn(0.f, 0.f);
+    if (gy < H && gx < W)
+      v = *reinterpret_cast<const __half2*>(in + (((long long)b * C + c0 + c) * H + gy) * W + gx);
+    s0[(y * kTX + 2 * xp) * kHP + c] = __low2half(v);
+    s0[(y * kTX + 2 * xp + 1) * kHP + c] = __high2half(v);
+  }
+  __syncthreads();
+  __half* pb = packed + (long long)b * g.batch_elems;
+  // level 0: one position per warp step, lanes = channel pairs
+  for (int p0 = warp; p0 < kTY * kTX; p0 += 8) {
+    const int y = p0 / kTX, x = p0 % kTX;
+    const int gy = ty0 + y, gx = tx0 + x;
+    if (gy < H && gx < W)
+      *reinterpret_cast<__half2*>(pb + g.off[0] + ((long long)gy * W + gx) * C + c0 + 2 * lane) =
+          *reinterpret_cast<const __half2*>(s0 + p0 * kHP + 2 * lane);
+  }
+  __half* src = s0;
+  __half* dst = s1;
+  int sx = kTX, sy = kTY;
+  for (int l = 1; l < nlev && l < kFusedLevels; ++l) {
+    const int ny = sy / 2, nx = sx / 2;
+    __syncthreads();
+    for (int i = tid; i < ny * nx * (kHC / 2); i += 256) {
+      const int cp = i % (kHC / 2), pp = i / (kHC / 2);
+      const int y = pp / nx, x = pp % nx;
+      const __half* q = src + ((2 * y) * sx + 2 * x) * kHP + 2 * cp;
+      const float2 a = __half22float2(*reinterpret_cast<const __half2*>(q));
+      const float2 bq = __half22float2(*reinterpret_cast<const __half2*>(q + kHP));
+      const float2 cq = __half22float2(*reinterpret_cast<const __half2*>(q + sx * kHP));
+      const float2 dq = __half22float2(*reinterpret_cast<const __half2*>(q + sx * kHP + kHP));
+      float ax = a.x, ay = a.y;
+      ax += bq.x; ay += bq.y;
+      ax += cq.x; ay += cq.y;
+      ax += dq.x; ay += dq.y;
+      *reinterpret_cast<__half2*>(dst + pp * kHP + 2 * cp) = __floats2half2_rn(ax / 4.f, ay / 4.f);
+    }
+    __syncthreads();
+    const int hl = g.h[l], wl = g.w[l];
+    const int oy = ty0 >> l, ox = tx0 >> l;
+    for (int pp = warp; pp < ny * nx; pp += 8) {
+      const int y = pp / nx, x = pp % nx;
+      const int gy = oy + y, gx = ox + x;
+      if (gy < hl && gx < wl)
+        *reinterpret_cast<__half2*>(pb + g.off[l] + ((long long)gy * wl + gx) * C + c0 + 2 * lane) =
+            *reinterpret_cast<const __half2*>(dst + pp * kHP + 2 * lane);
+    }
+    __half* t = src; src = dst; dst = t;
+    sy = ny; sx = nx;
+  }
+}
+
 template <typename T>
 __global__ void pool_level_kernel(T* __restrict__ packed, int C, PyrGeom g, int l) {
   const int hl = g.h[l], wl = g.w[l];
@@ -309,9 +382,16 @@ bool launch_build(const void* in, void* packed, int B, int C, int H, int W, int 
   const PyrGeom g = make_geom(H, W, C, levels);
   constexpr int CC = 32;  // 40 KB of static shared memory per CTA
   const int tiles = ((H + kTY - 1) / kTY) * ((W + kTX - 1) / kTX);
-  dim3 grid(tiles, (C + CC - 1) / CC, B);
-  pyramid_build_kernel<T, CC><<<grid, 256, 0, s>>>((const T*)in, (T*)packed, C, H, W, g,
-                                                   levels);
+  if (std::is_same<T, __half>::value && C % kHC == 0 && W % 2 == 0 &&
+      ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(packed)) & 3) == 0) {
+    dim3 grid(tiles, C / kHC, B);
+    pyramid_build_h_kernel<<<grid, 256, 0, s>>>((const __half*)in, (__half*)packed, C, H, W, g,
+                                                levels);
+  } else {
+    dim3 grid(tiles, (C + CC - 1) / CC, B);
+    pyramid_build_kernel<T, CC><<<grid, 256, 0, s>>>((const T*)in, (T*)packed, C, H, W, g,
+                                                     levels);
+  }
   count_launch();
   if (!check_launch("pyramid_build")) return false;
   for (int l = kFusedLevels; l < levels; ++l) {

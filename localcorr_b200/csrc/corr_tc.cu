@@ -864,6 +864,19 @@ __device__ __forceinline__ void pixel_coords(const TcBwdParams& p, int b, int pi
   }
 }
 
+// A grad_fmap1 row group (box rows gi*Rg.. of level l for the cell at
+// (cell_y0, cell_x0)) takes part only if it overlaps the level's map: outside
+// it the boxes are TMA zero fill and contribute nothing.
+__device__ __forceinline__ bool b1_group_live(const TcGeom& g, int l, int gi, int cell_y0,
+                                              int cell_x0, int radius) {
+  const int X0 = ((cell_x0 >> l) - radius) & ~7;
+  if (X0 >= g.w[l] || X0 + g.UWb[l] <= 0) return false;
+  const int Y0 = (cell_y0 >> l) - radius;
+  const int ra = Y0 + gi * g.Rg[l];
+  const int rb = min(ra + g.Rg[l], Y0 + g.UH[l]);
+  return ra < g.h[l] && rb > 0;
+}
+
 // grad_fmap1, per 128-pixel chunk: D[128 px x C] += G[128 px x 64 pos] *
 // F2[64 pos x C] over every union row group of every level; D lives in TMEM
 // for the whole chunk, so each pixel row is written once (no atomics).
@@ -935,9 +948,11 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
           const int X0 = ((cell_x0 >> l) - RADIUS) & ~7;
           const int Y0 = (cell_y0 >> l) - RADIUS;
           const uint32_t box = 128u * g.UWb[l] * g.Rg[l];
-          for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
+          for (int gi = 0; gi < g.ngroups[l]; ++gi) {
+            if (!b1_group_live(g, l, gi, cell_y0, cell_x0, RADIUS)) continue;
             const int s = gs % NST;
             const uint32_t use = gs / NST;
+            ++gs;
             if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
             tc::mbar_arrive_expect_tx(bfull + s, box * g.KC);
             uint8_t* sb = smem + (size_t)s * SB + 16384;
@@ -957,17 +972,24 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
       const uint32_t base = tc::smem_u32(smem);
       const uint32_t idesc = tc::idesc_f16_f32(128, g.C, false, true);
       bool ok = true;
+      int next_cell = blockIdx.x < nwork ? p.work[blockIdx.x].y : 0;
       for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
         const int buf = it & 1;
+        const int cell = next_cell;  // loaded one chunk ahead
+        if (wi + (int)gridDim.x < nwork) next_cell = p.work[wi + gridDim.x].y;
+        const int mcy = cell / g.ncx, mcx = cell - mcy * g.ncx;
+        const int m_y0 = g.ylo + mcy * kCellY, m_x0 = g.xlo + mcx * kCellX;
         if (!tc::mbar_wait(acc_empty + buf, ((it >> 1) & 1) ^ 1, abort)) break;
         tc::tc_fence_after();
         bool first = true;
         for (int l = 0; l < g.L && ok; ++l) {
           // K positions actually in the group's boxes: whole 16-row MMA steps
           const int nkk = (g.UWb[l] * g.Rg[l] + 15) / 16;
-          for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
+          for (int gi = 0; gi < g.ngroups[l]; ++gi) {
+            if (!b1_group_live(g, l, gi, m_y0, m_x0, RADIUS)) continue;
             const int s = gs % NST;
             const uint32_t use = gs / NST;
+            ++gs;
             if (!tc::mbar_wait(bfull + s, use & 1, abort) ||
                 !tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
             // A rows arrive through cp.async completion: make their
@@ -1018,10 +1040,12 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
         const int UPR = g.UWb[l] >> 3, Rg = g.Rg[l];
         const int nunit = 2 * ((g.UWb[l] * Rg + 15) / 16);  // A units the MMA reads
         const uint4* rec = p.gsh + ((long long)l * g.npix + idx) * (NG * NU);
-        for (int gi = 0; gi < g.ngroups[l]; ++gi, ++gs) {
-          if ((int)(gs % (uint32_t)p.nbg) != gb) continue;
-          const int s = gs % NST;
-          const uint32_t use = gs / NST;
+        for (int gi = 0; gi < g.ngroups[l]; ++gi) {
+          if (!b1_group_live(g, l, gi, cell_y0, cell_x0, RADIUS)) continue;
+          const uint32_t my = gs++;
+          if ((int)(my % (uint32_t)p.nbg) != gb) continue;
+          const int s = my % NST;
+          const uint32_t use = my / NST;
           if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
           // A row of this pixel: 8 units of 8 K positions (box row br, unit
           // uc of that row); each a record unit (cp.async) or zeros.
@@ -1057,12 +1081,26 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
       const int buf = it & 1;
       const bool valid = t < wk.w;
       const int gid = valid ? p.sorted[wk.z + t] : 0;
+      // A chunk whose boxes all lie off the map issued no MMA: its
+      // accumulator holds a previous chunk's values and its gradient is zero.
+      bool live = false;
+      {
+        const int ecy = wk.y / g.ncx, ecx = wk.y - ecy * g.ncx;
+        const int e_y0 = g.ylo + ecy * kCellY, e_x0 = g.xlo + ecx * kCellX;
+        for (int l = 0; l < g.L && !live; ++l)
+          for (int gi = 0; gi < g.ngroups[l] && !live; ++gi)
+            live = b1_group_live(g, l, gi, e_y0, e_x0, RADIUS);
+      }
       if (!tc::mbar_wait(acc_full + buf, (it >> 1) & 1, abort)) break;
       tc::tc_fence_after();
       for (int c0 = 0; c0 < g.C; c0 += 32) {
         float v[32];
         tc::tmem_ld32(lane_addr + buf * 256 + c0, v);
         tc::tmem_ld_wait();
+        if (!live) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = 0.f;
+        }
         if (valid) {
           uint4* dst = reinterpret_cast<uint4*>(p.grad_f1 + (long long)gid * g.C + c0);
 #pragma unroll

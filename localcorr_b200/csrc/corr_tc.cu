@@ -383,19 +383,30 @@ __global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* _
 
 // Sorted copy of fmap1 for the grad_fmap2 pull: row i = fmap1 row sorted[i]
 // for the sorted pixels, zeros for the rows past them (their A rows are zero
-// but the TMA tiles read them). One warp per row.
+// but the TMA tiles read them). One warp per kGatherRows rows, whose loads
+// are all issued before the stores.
+constexpr int kGatherRows = 4;
 __global__ void tc_gather_rows_kernel(const __half* __restrict__ fmap1, const int* __restrict__ sorted,
                                       const int* __restrict__ nsorted, __half* __restrict__ f1s,
                                       TcGeom g) {
-  const long long row = (long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const long long row0 =
+      ((long long)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5)) * kGatherRows;
   const int lane = threadIdx.x & 31;
-  if (row >= g.npix) return;
-  uint4* dst = reinterpret_cast<uint4*>(f1s + row * g.C);
-  if (row < *nsorted) {
-    const uint4* src = reinterpret_cast<const uint4*>(fmap1 + (long long)sorted[row] * g.C);
-    for (int i = lane; i < g.C / 8; i += 32) dst[i] = src[i];
-  } else {
-    for (int i = lane; i < g.C / 8; i += 32) dst[i] = make_uint4(0, 0, 0, 0);
+  const int ns = *nsorted;
+  const int units = g.C / 8;  // 16-byte units per row (<= 32)
+  if (lane >= units) return;
+  uint4 v[kGatherRows];
+#pragma unroll
+  for (int k = 0; k < kGatherRows; ++k) {
+    const long long row = row0 + k;
+    v[k] = make_uint4(0, 0, 0, 0);
+    if (row < ns)
+      v[k] = reinterpret_cast<const uint4*>(fmap1 + (long long)sorted[row] * g.C)[lane];
+  }
+#pragma unroll
+  for (int k = 0; k < kGatherRows; ++k) {
+    const long long row = row0 + k;
+    if (row < g.npix) reinterpret_cast<uint4*>(f1s + row * g.C)[lane] = v[k];
   }
 }
 
@@ -1819,7 +1830,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   TcWs W = ws_pointers(ws, L);
   if (!tc_sort(W, g, co, cdtype, s)) return false;
   {
-    const int rows_per_block = 8;
+    const int rows_per_block = 8 * kGatherRows;
     const long long nb = (g.npix + rows_per_block - 1) / rows_per_block;
     tc_gather_rows_kernel<<<(unsigned)nb, 32 * rows_per_block, 0, s>>>(
         static_cast<const __half*>(f1), W.sorted, W.offsets + (size_t)g.B * g.ncell * kColBins, W.f1s, g);

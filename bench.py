@@ -17,6 +17,13 @@ Metric: lookups = B*H*W*L*(2r+1)^2 per lookup call; value = Glookups/s of
 the whole job. Inputs (265 MB of maps + 2 GB of upstream gradients per GPU)
 are larger than L2, so no explicit flush is needed between steps.
 
+Workload raft_4k_rowband (benchmark configuration 4, forward only): one
+B=1, C=256, 270x480 frame with smooth flow (sinusoids up to 40 px), 24
+lookups per step, split into one row band per GPU (strong scaling): each rank
+builds its band's pyramid levels, one all-gather assembles the frame's
+pyramid on every rank (localcorr_b200.bands), and the lookups of the band run
+locally; value = the frame's lookups per second.
+
 The reference arm (--impl reference) times the reference's CPU path as
 restated in oracle/oracle.py (the all-pairs matmul + grid_sample formulation
 of onnx_generic.py:58-156) on the host cores, on a bounded sample.
@@ -48,6 +55,10 @@ CONFIGS = {
                           coords="uniform8", fdist="normal", backward=True),
     "raft_4k_inference": dict(B=1, C=256, H=270, W=480, L=4, r=4, iters=24, dtype="f16",
                               coords="smooth", fdist="normal", backward=False),
+    # the same 4K frame split into one row band per GPU (strong scaling): one
+    # all-gather of the band pyramids per frame, then 24 local lookups per band
+    "raft_4k_rowband": dict(B=1, C=256, H=270, W=480, L=4, r=4, iters=24, dtype="f16",
+                            coords="smooth", fdist="normal", backward=False, bands=True),
     "highbatch_r3": dict(B=8, C=128, H=64, W=128, L=4, r=3, iters=1, dtype="f16",
                          coords="uniform64", fdist="uniform", backward=True),
     "highbatch_r4": dict(B=8, C=128, H=64, W=128, L=4, r=4, iters=1, dtype="f16",
@@ -57,6 +68,11 @@ CONFIGS = {
 }
 DEFAULT = "raft_train_1080p"
 METRIC = "corr Glookups/s fwd+bwd (B*H*W*L*(2r+1)^2)"
+
+
+def metric_name(cfg):
+    """The headline metric; forward-only workloads count forward lookups."""
+    return METRIC if cfg["backward"] else METRIC.replace("fwd+bwd", "fwd")
 
 
 def _env_rank():
@@ -95,11 +111,15 @@ def lookups_per_call(cfg):
 
 
 def algorithmic_bytes(cfg, kernel):
-    """Bytes each tensor of one engine call occupies, touched once (storage dtype)."""
+    """Bytes each tensor of one engine call occupies, touched once (storage dtype).
+
+    A row band's call covers its rows of fmap1/coords/output and, of the
+    frame's pyramid, the band's share of the rows."""
     es = 2 if cfg["dtype"] == "f16" else 4
     b, c, h, w, L, r = cfg["B"], cfg["C"], cfg["H"], cfg["W"], cfg["L"], cfg["r"]
-    p = b * h * w
-    pyr = sum(b * (h >> l) * (w >> l) * c for l in range(L)) * es
+    rows = cfg.get("band_rows", h)
+    p = b * rows * w
+    pyr = sum(b * (h >> l) * (w >> l) * c for l in range(L)) * es * rows // max(1, h)
     f1 = p * c * es
     coords = 2 * p * es
     out = p * L * (2 * r + 1) ** 2 * es
@@ -179,27 +199,36 @@ class ClockSampler:
 
 
 def make_inputs(cfg, rank, device):
+    """Seeded synthetic inputs of one rank: its own batch shard, or (row-band
+    workloads, cfg["band"] = (y0, y1)) its rows of the one frame all ranks share."""
     from oracle import oracle
 
-    g = torch.Generator().manual_seed(1234 + rank)
+    seed = 0 if cfg.get("bands") else rank
+    g = torch.Generator().manual_seed(1234 + seed)
     dt = torch.float16 if cfg["dtype"] == "f16" else torch.float32
     b, c, h, w = cfg["B"], cfg["C"], cfg["H"], cfg["W"]
-    f1, f2 = oracle.make_fmaps(b, c, h, w, seed=1234 + rank, dist=cfg["fdist"])
+    f1, f2 = oracle.make_fmaps(b, c, h, w, seed=1234 + seed, dist=cfg["fdist"])
     kind = cfg["coords"]
     if kind == "gauss_oob":
-        c0 = oracle.make_coords_gauss_oob(b, h, w, 6.0, 0.05, seed=99 + rank)
+        c0 = oracle.make_coords_gauss_oob(b, h, w, 6.0, 0.05, seed=99 + seed)
     elif kind == "smooth":
-        c0 = oracle.make_coords_smooth(b, h, w, 40.0, seed=99 + rank)
+        c0 = oracle.make_coords_smooth(b, h, w, 40.0, seed=99 + seed)
     elif kind == "uniform64":
-        c0 = oracle.make_coords_uniform(b, h, w, 64.0, seed=99 + rank)
+        c0 = oracle.make_coords_uniform(b, h, w, 64.0, seed=99 + seed)
     else:
-        c0 = oracle.make_coords_uniform(b, h, w, 8.0, seed=99 + rank)
+        c0 = oracle.make_coords_uniform(b, h, w, 8.0, seed=99 + seed)
     coords = []
     for i in range(cfg["iters"]):
         if i == 0:
             coords.append(c0)
         else:
             coords.append(coords[-1] + torch.randn(c0.shape, generator=g))
+    if cfg.get("bands"):
+        y0, y1 = cfg["band"]
+        f1 = f1[:, :, y0:y1].contiguous()
+        f2 = f2[:, :, y0:y1].contiguous()
+        coords = [co[:, :, y0:y1].contiguous() for co in coords]
+        h = y1 - y0
     rd = 2 * cfg["r"] + 1
     grads = None
     if cfg["backward"]:
@@ -221,6 +250,14 @@ def make_inputs(cfg, rank, device):
 def run_step(cfg, f1, f2, coords, grads):
     import localcorr_b200 as lc
 
+    if cfg.get("bands"):
+        from localcorr_b200 import bands
+
+        with torch.no_grad():
+            block = bands.LocalCorrRowBandBlock(f1, f2, cfg["H"], num_levels=cfg["L"],
+                                                radius=cfg["r"])
+            outs = [block(co) for co in coords]
+        return outs[-1], None
     if cfg["backward"]:
         f1 = f1.detach().requires_grad_(True)
         f2 = f2.detach().requires_grad_(True)
@@ -288,7 +325,7 @@ def reference_arm(args, cfg, cfg_name):
         t_total += s["seconds"]
     v = statistics.median(vals)
     line = {
-        "impl": "reference", "metric": METRIC, "value": v, "unit": "Glookups/s",
+        "impl": "reference", "metric": metric_name(cfg), "value": v, "unit": "Glookups/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * t_total / max(1, args.steps), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -319,6 +356,11 @@ def main(argv=None):
         return reference_arm(args, cfg, args.config)
 
     rank, local_rank, world = _env_rank()
+    if cfg.get("bands"):
+        from localcorr_b200 import bands
+
+        cfg["band"] = bands.band_rows(cfg["H"], world, 1 << (cfg["L"] - 1))[rank]
+        cfg["band_rows"] = cfg["band"][1] - cfg["band"][0]
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
     dist = None
@@ -428,8 +470,9 @@ def main(argv=None):
     e2e_elapsed = max_over_ranks(e2e_elapsed, dist, device)
 
     lookups_step = lookups_per_call(cfg) * cfg["iters"]
-    value = lookups_step * args.steps * world / elapsed / 1e9
-    e2e_value = lookups_step * args.steps * world / e2e_elapsed / 1e9
+    shards = 1 if cfg.get("bands") else world  # row bands split one frame
+    value = lookups_step * args.steps * shards / elapsed / 1e9
+    e2e_value = lookups_step * args.steps * shards / e2e_elapsed / 1e9
     h2d = (host["f1"].numel() + host["f2"].numel()) * host["f1"].element_size() + sum(
         co.numel() * co.element_size() for co in host["coords"])
 
@@ -456,16 +499,18 @@ def main(argv=None):
             cpu = cpu_baseline_sample(cfg)
             cpu.pop("seconds", None)
         line = {
-            "metric": METRIC, "value": value, "unit": "Glookups/s", "n_gpus": world,
+            "metric": metric_name(cfg), "value": value, "unit": "Glookups/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup),
             "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong" if cfg.get("bands") else "weak", "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic",
             "config": {"workload": args.config, "B_per_gpu": cfg["B"], "global_batch":
-                       cfg["B"] * world, "C": cfg["C"], "H": cfg["H"], "W": cfg["W"],
+                       cfg["B"] * shards, "C": cfg["C"], "H": cfg["H"], "W": cfg["W"],
                        "levels": cfg["L"], "radius": cfg["r"], "lookups_per_step":
                        cfg["iters"], "backward": cfg["backward"],
-                       "parallelism": f"batch-shard x{world}, no collective",
+                       "parallelism": (f"row-band x{world}: one all-gather of the band "
+                                       "pyramids per frame" if cfg.get("bands") else
+                                       f"batch-shard x{world}, no collective"),
                        "l2": "inputs larger than L2 (no flush)"},
             "e2e": {"value": e2e_value, "unit": "Glookups/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 8,

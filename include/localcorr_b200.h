@@ -114,6 +114,32 @@ LCB200_API bool launchLocalCorrB200PyramidBackward(
     int dtype, int coords_dtype, bool ymajor, float scale, int accumulate, int engine,
     void* workspace, size_t workspace_bytes, cudaStream_t stream);
 
+/* ---- Separate map size (no reference counterpart: the reference derives the
+ * pyramid from fmap1's H1 x W1) ---------------------------------------------
+ * The three calls above with the pixel grid (fmap1, coords, corr, corr_grad:
+ * H1 x W1) decoupled from the level-0 size of the map fmap2_packed was built
+ * from (H2 x W2; level l is (H2 >> l) x (W2 >> l)). coords stay in level-0
+ * pixels of the map. A row band of a large frame (rows [y0, y1) of fmap1 and
+ * coords, H1 = y1 - y0) against the whole frame's pyramid (H2 = H) gives
+ * exactly rows [y0, y1) of the whole-frame output, which is how one frame is
+ * split over several GPUs. With H2 = H1 and W2 = W1 they are the calls
+ * above. */
+LCB200_API size_t localCorrB200PyramidWorkspaceBytesMapDims(
+    int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int dilation, int dtype, int engine);
+LCB200_API bool launchLocalCorrB200PyramidForwardMapDims(
+    const void* fmap1, const void* fmap2_packed, const void* coords, void* corr,
+    int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int dilation, int dtype, int coords_dtype, bool ymajor, float scale,
+    int engine, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+LCB200_API bool launchLocalCorrB200PyramidBackwardMapDims(
+    const void* fmap1, const void* fmap2_packed, const void* coords,
+    const void* corr_grad, void* fmap1_grad, float* fmap2_grad_f32,
+    int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int dilation, int dtype, int coords_dtype, bool ymajor, float scale,
+    int accumulate, int engine, void* workspace, size_t workspace_bytes,
+    cudaStream_t stream);
+
 /* ---- Allocation-free forward (no counterpart in the reference) -------------
  * Some callers may not allocate device memory at the time they run the
  * correlation: a TensorRT plugin's enqueue (the engine's memory is fixed when

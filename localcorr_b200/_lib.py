@@ -54,6 +54,19 @@ PROTOTYPES = {
         + [_c_int] * 7
         + [_c_int, _c_int, _c_bool, _c_float, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p],
     ),
+    "localCorrB200PyramidWorkspaceBytesMapDims": (_c_size_t, [_c_int] * 11),
+    "launchLocalCorrB200PyramidForwardMapDims": (
+        _c_bool,
+        [_c_void_p] * 4
+        + [_c_int] * 9
+        + [_c_int, _c_int, _c_bool, _c_float, _c_int, _c_void_p, _c_size_t, _c_void_p],
+    ),
+    "launchLocalCorrB200PyramidBackwardMapDims": (
+        _c_bool,
+        [_c_void_p] * 6
+        + [_c_int] * 9
+        + [_c_int, _c_int, _c_bool, _c_float, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p],
+    ),
     "launchLocalCorrB200PyramidForwardNoAlloc": (
         _c_bool,
         [_c_void_p] * 4 + [_c_int] * 6 + [_c_int, _c_int, _c_bool, _c_float, _c_void_p],

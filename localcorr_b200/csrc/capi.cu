@@ -10,19 +10,26 @@
 namespace lcb200 {
 
 // Engines (defined in corr_simt.cu, corr_tc.cu, layout.cu, spatial.cu).
-bool simt_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
-                  int, int, int, bool, float, cudaStream_t);
-bool simt_backward(const void*, const void*, const void*, const void*, void*, float*, int,
-                   int, int, int, int, int, int, int, int, bool, float, bool, cudaStream_t);
-bool tc_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
-                 int dtype, std::string* why);
-size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels, bool backward);
-bool tc_forward(const void*, const void*, const void*, void*, int, int, int, int, int, int,
-                int, bool, float, void*, size_t, cudaStream_t);
-bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int, int,
-                 int, int, int, int, int, bool, float, bool, void*, size_t, cudaStream_t);
-bool tc_bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
-                     int dtype, std::string* why);
+// (H1, W1) is the pixel grid of fmap1/coords/corr, (H2, W2) the level-0 size
+// of the map fmap2_packed was built from.
+bool simt_forward(const void*, const void*, const void*, void*, int B, int H1, int W1, int H2,
+                  int W2, int C, int r, int levels, int dil, int dtype, int cdtype, bool ymajor,
+                  float scale, cudaStream_t);
+bool simt_backward(const void*, const void*, const void*, const void*, void*, float*, int B,
+                   int H1, int W1, int H2, int W2, int C, int r, int levels, int dil, int dtype,
+                   int cdtype, bool ymajor, float scale, bool acc1, cudaStream_t);
+bool tc_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                 int dilation, int dtype, std::string* why);
+size_t tc_workspace_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                          bool backward);
+bool tc_forward(const void*, const void*, const void*, void*, int B, int H1, int W1, int H2,
+                int W2, int C, int radius, int levels, int cdtype, bool ymajor, float scale,
+                void*, size_t, cudaStream_t);
+bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int B,
+                 int H1, int W1, int H2, int W2, int C, int radius, int levels, int cdtype,
+                 bool ymajor, float scale, bool acc_f1, void*, size_t, cudaStream_t);
+bool tc_bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                     int dilation, int dtype, std::string* why);
 int tc_device_status(bool reset);
 bool layout_nchw_to_nhwc(const void*, void*, int, int, int, int, cudaStream_t);
 bool layout_nhwc_to_nchw(const void*, void*, int, int, int, int, cudaStream_t);
@@ -91,8 +98,8 @@ namespace {
 // launchers (cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:1420-1435) plus the
 // checks the reference leaves implicit (non-negative radius, positive C,
 // 32-bit index ranges).
-bool validate_pyramid(int B, int H1, int W1, int C, int radius, int levels, int dilation,
-                      int dtype, bool* empty) {
+bool validate_pyramid(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                      int dilation, int dtype, bool* empty) {
   *empty = false;
   if ((long long)H1 * W1 <= 0 || B <= 0) { *empty = true; return true; }
   if (levels < 1 || levels > kMaxLevels) {
@@ -116,14 +123,14 @@ bool validate_pyramid(int B, int H1, int W1, int C, int radius, int levels, int 
     return false;
   }
   for (int l = 0; l < levels; ++l) {
-    if ((H1 >> l) < 1 || (W1 >> l) < 1) {
-      set_error("level " + std::to_string(l) + " of a " + std::to_string(H1) + "x" +
-                std::to_string(W1) + " map is empty");
+    if ((H2 >> l) < 1 || (W2 >> l) < 1) {
+      set_error("level " + std::to_string(l) + " of a " + std::to_string(H2) + "x" +
+                std::to_string(W2) + " map is empty");
       return false;
     }
   }
-  if ((long long)H1 * W1 > (1ll << 30)) {
-    set_error("H1*W1 too large");
+  if ((long long)H1 * W1 > (1ll << 30) || (long long)H2 * W2 > (1ll << 30)) {
+    set_error("H1*W1 or H2*W2 too large");
     return false;
   }
   return true;
@@ -162,14 +169,16 @@ void* library_scratch(size_t bytes, cudaStream_t s) {
   return p;
 }
 
-bool use_tc(int engine, int B, int H1, int W1, int C, int radius, int levels, int dilation,
+bool use_tc(int engine, int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+            int dilation,
             int dtype, bool* ok, bool backward = false, const void* p1 = nullptr,
             const void* p2 = nullptr) {
   *ok = true;
   if (engine == LCB200_ENGINE_SIMT) return false;
   std::string why;
-  bool elig = backward ? tc_bwd_eligible(B, H1, W1, C, radius, levels, dilation, dtype, &why)
-                       : tc_eligible(B, H1, W1, C, radius, levels, dilation, dtype, &why);
+  bool elig = backward
+                  ? tc_bwd_eligible(B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &why)
+                  : tc_eligible(B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &why);
   // TMA and 16-byte cp.async need 16-byte aligned map bases.
   if (elig && ((reinterpret_cast<uintptr_t>(p1) | reinterpret_cast<uintptr_t>(p2)) & 15)) {
     elig = false;
@@ -189,20 +198,20 @@ bool use_tc(int engine, int B, int H1, int W1, int C, int radius, int levels, in
 }
 
 bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1,
-                     int W1, int C, int radius, int levels, int dil, int dtype, int cdtype,
+                     int W1, int H2, int W2, int C, int radius, int levels, int dil, int dtype, int cdtype,
                      bool ymajor, float scale, int engine, void* ws, size_t ws_bytes,
                      bool lib_ws, cudaStream_t s) {
   clear_error();
   bool empty = false;
-  if (!validate_pyramid(B, H1, W1, C, radius, levels, dil, dtype, &empty)) return false;
+  if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &empty)) return false;
   if (empty) return true;
   if (cdtype != LCB200_F32 && cdtype != LCB200_F16) {
     set_error("coords dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
     return false;
   }
   bool ok = true;
-  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok, false, f1, f2)) {
-    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels, false);
+  if (use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &ok, false, f1, f2)) {
+    const size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, false);
     if (lib_ws) {
       ws = library_scratch(need, s);
       ws_bytes = ws ? need : 0;
@@ -212,22 +221,23 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
                 std::to_string(ws_bytes));
       return false;
     }
-    return tc_forward(f1, f2, co, out, B, H1, W1, C, radius, levels, cdtype, ymajor, scale, ws,
-                      ws_bytes, s);
+    return tc_forward(f1, f2, co, out, B, H1, W1, H2, W2, C, radius, levels, cdtype, ymajor,
+                      scale, ws, ws_bytes, s);
   }
   if (!ok) return false;
-  return simt_forward(f1, f2, co, out, B, H1, W1, C, radius, levels, dil, dtype, cdtype, ymajor,
-                      scale, s);
+  return simt_forward(f1, f2, co, out, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, cdtype,
+                      ymajor, scale, s);
 }
 
 bool pyramid_backward(const void* f1, const void* f2, const void* co, const void* gout,
-                      void* f1g, float* f2g, int B, int H1, int W1, int C, int radius,
+                      void* f1g, float* f2g, int B, int H1, int W1, int H2, int W2, int C,
+                      int radius,
                       int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
                       int accumulate, int engine, void* ws, size_t ws_bytes, bool lib_ws,
                       cudaStream_t s) {
   clear_error();
   bool empty = false;
-  if (!validate_pyramid(B, H1, W1, C, radius, levels, dil, dtype, &empty)) return false;
+  if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &empty)) return false;
   if (empty) return true;
   if (cdtype != LCB200_F32 && cdtype != LCB200_F16) {
     set_error("coords dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
@@ -235,13 +245,13 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
   }
   const bool acc1 = (accumulate & LCB200_ACC_FMAP1) != 0;
   if (!(accumulate & LCB200_ACC_FMAP2)) {
-    const PyrGeom g = make_geom(H1, W1, C, levels);
+    const PyrGeom g = make_geom(H2, W2, C, levels);
     if (cudaMemsetAsync(f2g, 0, sizeof(float) * (size_t)B * g.batch_elems, s) != cudaSuccess)
       return check_launch("memset fmap2_grad");
   }
   bool ok = true;
-  if (use_tc(engine, B, H1, W1, C, radius, levels, dil, dtype, &ok, true, f1, f2)) {
-    const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels, true);
+  if (use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &ok, true, f1, f2)) {
+    const size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, true);
     if (lib_ws) {
       ws = library_scratch(need, s);
       ws_bytes = ws ? need : 0;
@@ -251,12 +261,12 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
                 std::to_string(ws_bytes));
       return false;
     }
-    return tc_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, radius, levels, cdtype, ymajor,
-                       scale, acc1, ws, ws_bytes, s);
+    return tc_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels, cdtype,
+                       ymajor, scale, acc1, ws, ws_bytes, s);
   }
   if (!ok) return false;
-  return simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, radius, levels, dil, dtype,
-                       cdtype, ymajor, scale, acc1, s);
+  return simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels, dil,
+                       dtype, cdtype, ymajor, scale, acc1, s);
 }
 
 bool validate_layout(int B, int C, int H, int W, int dtype) {
@@ -282,8 +292,8 @@ bool launchLocalCorrCudaPyramidForward(const void* fmap1, const void* fmap2_pack
                                        const void* coords, void* corr, int B, int H1, int W1,
                                        int C, int radius, int levels, int dilation, bool isHalf,
                                        bool ymajor, cudaStream_t stream) {
-  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, C, radius, levels,
-                         dilation, isHalf ? LCB200_F16 : LCB200_F32,
+  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H1, W1, C, radius,
+                         levels, dilation, isHalf ? LCB200_F16 : LCB200_F32,
                          isHalf ? LCB200_F16 : LCB200_F32, ymajor, 1.0f, LCB200_ENGINE_AUTO,
                          nullptr, 0, true, stream);
 }
@@ -294,23 +304,32 @@ bool launchLocalCorrCudaPyramidBackward(const void* fmap1, const void* fmap2_pac
                                         int W1, int C, int radius, int levels, int dilation,
                                         bool isHalf, bool ymajor, cudaStream_t stream) {
   return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad, B, H1,
-                          W1, C, radius, levels, dilation, isHalf ? LCB200_F16 : LCB200_F32,
+                          W1, H1, W1, C, radius, levels, dilation,
+                          isHalf ? LCB200_F16 : LCB200_F32,
                           isHalf ? LCB200_F16 : LCB200_F32, ymajor, 1.0f, LCB200_ACC_FMAP2,
                           LCB200_ENGINE_AUTO, nullptr, 0, true, stream);
 }
 
-size_t localCorrB200PyramidWorkspaceBytes(int B, int H1, int W1, int C, int radius, int levels,
-                                          int dilation, int dtype, int engine) {
+size_t localCorrB200PyramidWorkspaceBytesMapDims(int B, int H1, int W1, int H2, int W2, int C,
+                                                 int radius, int levels, int dilation,
+                                                 int dtype, int engine) {
   bool empty = false;
   clear_error();
-  if (!validate_pyramid(B, H1, W1, C, radius, levels, dilation, dtype, &empty) || empty)
+  if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &empty) || empty)
     return 0;
   bool ok = true;
-  const bool f = use_tc(engine, B, H1, W1, C, radius, levels, dilation, dtype, &ok);
+  const bool f = use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &ok);
   ok = true;
-  const bool b = use_tc(engine, B, H1, W1, C, radius, levels, dilation, dtype, &ok, true);
+  const bool b =
+      use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &ok, true);
   if (!f && !b) return 0;
-  return tc_workspace_bytes(B, H1, W1, C, radius, levels, b);
+  return tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, b);
+}
+
+size_t localCorrB200PyramidWorkspaceBytes(int B, int H1, int W1, int C, int radius, int levels,
+                                          int dilation, int dtype, int engine) {
+  return localCorrB200PyramidWorkspaceBytesMapDims(B, H1, W1, H1, W1, C, radius, levels,
+                                                   dilation, dtype, engine);
 }
 
 bool launchLocalCorrB200PyramidForward(const void* fmap1, const void* fmap2_packed,
@@ -319,8 +338,20 @@ bool launchLocalCorrB200PyramidForward(const void* fmap1, const void* fmap2_pack
                                        int coords_dtype, bool ymajor, float scale, int engine,
                                        void* workspace, size_t workspace_bytes,
                                        cudaStream_t stream) {
-  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, C, radius, levels,
-                         dilation, dtype, coords_dtype, ymajor, scale, engine, workspace,
+  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H1, W1, C, radius,
+                         levels, dilation, dtype, coords_dtype, ymajor, scale, engine, workspace,
+                         workspace_bytes, false, stream);
+}
+
+bool launchLocalCorrB200PyramidForwardMapDims(const void* fmap1, const void* fmap2_packed,
+                                              const void* coords, void* corr, int B, int H1,
+                                              int W1, int H2, int W2, int C, int radius,
+                                              int levels, int dilation, int dtype,
+                                              int coords_dtype, bool ymajor, float scale,
+                                              int engine, void* workspace,
+                                              size_t workspace_bytes, cudaStream_t stream) {
+  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H2, W2, C, radius,
+                         levels, dilation, dtype, coords_dtype, ymajor, scale, engine, workspace,
                          workspace_bytes, false, stream);
 }
 
@@ -332,15 +363,27 @@ bool launchLocalCorrB200PyramidBackward(const void* fmap1, const void* fmap2_pac
                                         int accumulate, int engine, void* workspace,
                                         size_t workspace_bytes, cudaStream_t stream) {
   return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad_f32, B,
-                          H1, W1, C, radius, levels, dilation, dtype, coords_dtype, ymajor,
-                          scale, accumulate, engine, workspace, workspace_bytes, false, stream);
+                          H1, W1, H1, W1, C, radius, levels, dilation, dtype, coords_dtype,
+                          ymajor, scale, accumulate, engine, workspace, workspace_bytes, false,
+                          stream);
+}
+
+bool launchLocalCorrB200PyramidBackwardMapDims(
+    const void* fmap1, const void* fmap2_packed, const void* coords, const void* corr_grad,
+    void* fmap1_grad, float* fmap2_grad_f32, int B, int H1, int W1, int H2, int W2, int C,
+    int radius, int levels, int dilation, int dtype, int coords_dtype, bool ymajor, float scale,
+    int accumulate, int engine, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad_f32, B,
+                          H1, W1, H2, W2, C, radius, levels, dilation, dtype, coords_dtype,
+                          ymajor, scale, accumulate, engine, workspace, workspace_bytes, false,
+                          stream);
 }
 
 bool launchLocalCorrB200PyramidBuild(const void* fmap2_nchw, void* fmap2_packed, int B, int C,
                                      int H, int W, int levels, int dtype, cudaStream_t stream) {
   clear_error();
   bool empty = false;
-  if (!validate_pyramid(B, H, W, C, 0, levels, 1, dtype, &empty)) return false;
+  if (!validate_pyramid(B, H, W, H, W, C, 0, levels, 1, dtype, &empty)) return false;
   if (empty) return true;
   return layout_pyramid_build(fmap2_nchw, fmap2_packed, B, C, H, W, levels, dtype, stream);
 }
@@ -350,7 +393,7 @@ bool launchLocalCorrB200PyramidBuildBackward(const void* grad_packed, bool grad_
                                              int levels, int dtype, cudaStream_t stream) {
   clear_error();
   bool empty = false;
-  if (!validate_pyramid(B, H, W, C, 0, levels, 1, dtype, &empty)) return false;
+  if (!validate_pyramid(B, H, W, H, W, C, 0, levels, 1, dtype, &empty)) return false;
   if (empty) return true;
   return layout_pyramid_build_grad(grad_packed, grad_is_f32, grad_fmap2_nchw, B, C, H, W,
                                    levels, dtype, stream);

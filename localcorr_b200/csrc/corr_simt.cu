@@ -302,9 +302,9 @@ bool launch_bwd(const void* f1, const void* f2, const void* co, const void* gout
 // Host entry: forward of the SIMT engine. Chooses 4 pixels per warp when the
 // shared-memory footprint allows it, else 1.
 bool simt_forward(const void* f1, const void* f2, const void* co, void* out, int B,
-                  int H1, int W1, int C, int r, int levels, int dil, int dtype, int cdtype,
-                  bool ymajor, float scale, cudaStream_t s) {
-  const PyrGeom g = make_geom(H1, W1, C, levels);
+                  int H1, int W1, int H2, int W2, int C, int r, int levels, int dil, int dtype,
+                  int cdtype, bool ymajor, float scale, cudaStream_t s) {
+  const PyrGeom g = make_geom(H2, W2, C, levels);
   const int RD = 2 * r + 1;
   const int NX = (dil == 1) ? RD + 1 : 2 * RD;
   const size_t lim = (size_t)max_dyn_smem();
@@ -333,10 +333,10 @@ bool simt_forward(const void* f1, const void* f2, const void* co, void* out, int
 }
 
 bool simt_backward(const void* f1, const void* f2, const void* co, const void* gout,
-                   void* f1g, float* f2g, int B, int H1, int W1, int C, int r,
-                   int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
+                   void* f1g, float* f2g, int B, int H1, int W1, int H2, int W2, int C,
+                   int r, int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
                    bool acc1, cudaStream_t s) {
-  const PyrGeom g = make_geom(H1, W1, C, levels);
+  const PyrGeom g = make_geom(H2, W2, C, levels);
   const int RD = 2 * r + 1;
   const int NX = (dil == 1) ? RD + 1 : 2 * RD;
   const size_t lim = (size_t)max_dyn_smem();

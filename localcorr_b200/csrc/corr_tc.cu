@@ -98,7 +98,8 @@ struct TcGeom {
 inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 inline int round_up(int a, int b) { return ceil_div(a, b) * b; }
 
-bool make_tc_geom(int B, int H, int W, int C, int r, int L, TcGeom* g, std::string* why) {
+bool make_tc_geom(int B, int H, int W, int H2, int W2, int C, int r, int L, TcGeom* g,
+                  std::string* why) {
   TcGeom t{};
   t.B = B; t.H = H; t.W = W; t.C = C; t.r = r; t.L = L;
   t.RD = 2 * r + 1;
@@ -111,15 +112,15 @@ bool make_tc_geom(int B, int H, int W, int C, int r, int L, TcGeom* g, std::stri
   // Bases outside [lo, hi) have windows outside the map at every level.
   t.ylo = -round_up((r + 2) * s, kCellY);
   t.xlo = -round_up((r + 2) * s, kCellX);
-  t.yhi = H + (r + 1) * s;
-  t.xhi = W + (r + 1) * s;
+  t.yhi = H2 + (r + 1) * s;
+  t.xhi = W2 + (r + 1) * s;
   t.ncy = ceil_div(t.yhi - t.ylo, kCellY);
   t.ncx = ceil_div(t.xhi - t.xlo, kCellX);
   t.ncell = t.ncy * t.ncx;
   long long acc = 0;
   for (int l = 0; l < L; ++l) {
-    t.h[l] = H >> l;
-    t.w[l] = W >> l;
+    t.h[l] = H2 >> l;
+    t.w[l] = W2 >> l;
     t.off[l] = acc;
     acc += (long long)C * t.h[l] * t.w[l];
   }
@@ -1619,8 +1620,9 @@ size_t fwd_smem_bytes(const TcGeom& g, int nstage, uint32_t* stage_bytes) {
 
 bool radius_supported(int r) { return r == 3 || r == 4 || r == 8; }
 
-bool eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation, int dtype,
-              std::string* why, TcGeom* out_geom, int* out_nstage) {
+bool eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+              int dilation, int dtype, std::string* why, TcGeom* out_geom,
+              int* out_nstage) {
   auto no = [&](const char* m) { if (why) *why = m; return false; };
   if (dtype != LCB200_F16) return no("tensor-core engine needs float16 maps");
   if (dilation != 1) return no("tensor-core engine needs dilation 1");
@@ -1628,7 +1630,7 @@ bool eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation
   if (C % 64 != 0 || C < 64 || C > 256) return no("tensor-core engine needs C in {64,128,192,256}");
   if (!radius_supported(radius)) return no("tensor-core engine radius not instantiated");
   TcGeom g;
-  if (!make_tc_geom(B, H1, W1, C, radius, levels, &g, why)) return false;
+  if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, why)) return false;
   if ((long long)B * H1 * W1 >= (1ll << 31)) return no("too many pixels");
   const size_t lim = (size_t)max_dyn_smem();
   int nst = 4;
@@ -1650,25 +1652,26 @@ bool launch_fwd_kernel(const TcFwdParams& prm, size_t smem, cudaStream_t s) {
 
 }  // namespace
 
-bool tc_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation, int dtype,
-                 std::string* why) {
-  return eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, nullptr, nullptr);
+bool tc_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                 int dilation, int dtype, std::string* why) {
+  return eligible(B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, why, nullptr, nullptr);
 }
 
-size_t tc_workspace_bytes(int B, int H1, int W1, int C, int radius, int levels, bool backward) {
+size_t tc_workspace_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                          bool backward) {
   TcGeom g;
-  if (!make_tc_geom(B, H1, W1, C, radius, levels, &g, nullptr)) return 0;
+  if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, nullptr)) return 0;
   const WsLayout L = ws_layout(g);
   return backward ? L.total : L.fwd_total;
 }
 
 bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1, int W1,
-                int C, int radius, int levels, int cdtype, bool ymajor, float scale, void* ws,
+                int H2, int W2, int C, int radius, int levels, int cdtype, bool ymajor, float scale, void* ws,
                 size_t ws_bytes, cudaStream_t s) {
   TcGeom g;
   int nst = 0;
   std::string why;
-  if (!eligible(B, H1, W1, C, radius, levels, 1, LCB200_F16, &why, &g, &nst)) {
+  if (!eligible(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &why, &g, &nst)) {
     set_error("tensor-core forward: " + why);
     return false;
   }
@@ -1750,11 +1753,12 @@ int pick_stages(size_t stage, size_t extra, int maxst) {
   return n;
 }
 
-bool bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation, int dtype,
-                  std::string* why, TcGeom* out, int* nst1, int* nst2) {
+bool bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                  int dilation, int dtype, std::string* why, TcGeom* out, int* nst1,
+                  int* nst2) {
   TcGeom g;
   int nf = 0;
-  if (!eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, &g, &nf)) return false;
+  if (!eligible(B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, why, &g, &nf)) return false;
   const int nbg = 2;
   const int n1 = pick_stages(bwd1_stage_bytes(g), 256, 4);
   const int n2 = pick_stages(bwd2_stage_bytes(g), kBwd2Extra, 8);
@@ -1800,20 +1804,20 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
 
 }  // namespace
 
-bool tc_bwd_eligible(int B, int H1, int W1, int C, int radius, int levels, int dilation,
-                     int dtype, std::string* why) {
-  return bwd_eligible(B, H1, W1, C, radius, levels, dilation, dtype, why, nullptr, nullptr,
+bool tc_bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                     int dilation, int dtype, std::string* why) {
+  return bwd_eligible(B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, why, nullptr, nullptr,
                       nullptr);
 }
 
 bool tc_backward(const void* f1, const void* f2, const void* co, const void* gout, void* f1g,
-                 float* f2g, int B, int H1, int W1, int C, int radius, int levels, int cdtype,
-                 bool ymajor, float scale, bool acc_f1, void* ws, size_t ws_bytes,
-                 cudaStream_t s) {
+                 float* f2g, int B, int H1, int W1, int H2, int W2, int C, int radius,
+                 int levels, int cdtype, bool ymajor, float scale, bool acc_f1, void* ws,
+                 size_t ws_bytes, cudaStream_t s) {
   TcGeom g;
   int n1 = 0, n2 = 0;
   std::string why;
-  if (!bwd_eligible(B, H1, W1, C, radius, levels, 1, LCB200_F16, &why, &g, &n1, &n2)) {
+  if (!bwd_eligible(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &why, &g, &n1, &n2)) {
     set_error("tensor-core backward: " + why);
     return false;
   }
@@ -1974,7 +1978,7 @@ extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
     return false;
   }
   std::string why;
-  if (!tc_eligible(B, H1, W1, C, radius, levels, 1, dtype, &why)) {
+  if (!tc_eligible(B, H1, W1, H1, W1, C, radius, levels, 1, dtype, &why)) {
     set_error("no-alloc forward supports only tensor-core configurations: " + why);
     return false;
   }
@@ -1982,7 +1986,7 @@ extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
     set_error("no-alloc forward: maps must be 16-byte aligned");
     return false;
   }
-  const size_t need = tc_workspace_bytes(B, H1, W1, C, radius, levels, false);
+  const size_t need = tc_workspace_bytes(B, H1, W1, H1, W1, C, radius, levels, false);
   if (need > LCB200_NOALLOC_SCRATCH_BYTES) {
     set_error("no-alloc forward: this problem needs " + std::to_string(need) +
               " bytes of scratch, more than the fixed " +
@@ -1993,6 +1997,6 @@ extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
   }
   void* ws = noalloc_scratch_ptr();
   if (!ws) return false;
-  return tc_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, C, radius, levels,
+  return tc_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H1, W1, C, radius, levels,
                     coords_dtype, ymajor, scale, ws, LCB200_NOALLOC_SCRATCH_BYTES, stream);
 }

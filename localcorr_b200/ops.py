@@ -133,10 +133,31 @@ def pyramid_build_backward(grad_packed: torch.Tensor, shape, levels: int,
     return out
 
 
-def workspace_bytes(b, h, w, c, radius, levels, dilation, dtype_code, engine) -> int:
+def workspace_bytes(b, h, w, c, radius, levels, dilation, dtype_code, engine,
+                    map_hw=None) -> int:
     lib = _lib.require_library()
+    if map_hw is not None:
+        return int(lib.localCorrB200PyramidWorkspaceBytesMapDims(
+            b, h, w, map_hw[0], map_hw[1], c, radius, levels, dilation, dtype_code, engine))
     return int(lib.localCorrB200PyramidWorkspaceBytes(b, h, w, c, radius, levels, dilation,
                                                       dtype_code, engine))
+
+
+def _map_dims(fmap1, fmap2_packed, levels, map_hw):
+    """(H2, W2) of the map behind fmap2_packed, or None when it is fmap1's grid.
+
+    map_hw decouples the pyramid's level-0 size from fmap1's pixel grid (the
+    ``...MapDims`` entry points): a row band of fmap1/coords against a whole
+    frame's pyramid."""
+    b, h, w, c = fmap1.shape
+    if map_hw is None or (int(map_hw[0]), int(map_hw[1])) == (h, w):
+        return None
+    h2, w2 = int(map_hw[0]), int(map_hw[1])
+    if fmap2_packed.numel() != b * packed_row_elems(c, h2, w2, levels):
+        raise RuntimeError(
+            f"fmap2_packed has {fmap2_packed.numel()} elements; a {levels}-level pyramid of "
+            f"a {h2}x{w2} map with B={b}, C={c} has {b * packed_row_elems(c, h2, w2, levels)}")
+    return h2, w2
 
 
 def _workspace(t: torch.Tensor, nbytes: int):
@@ -147,37 +168,50 @@ def _workspace(t: torch.Tensor, nbytes: int):
 
 
 def pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation=1,
-                         ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO) -> torch.Tensor:
-    """corr [B, L, RD^2, H, W] = scale * local correlation (extended C ABI)."""
+                         ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO,
+                         map_hw=None) -> torch.Tensor:
+    """corr [B, L, RD^2, H, W] = scale * local correlation (extended C ABI).
+
+    ``map_hw=(H2, W2)``: fmap2_packed is the pyramid of an H2 x W2 map while
+    fmap1/coords/corr cover an H x W pixel grid (``...MapDims`` entry)."""
     lib = _lib.require_library()
     b, h, w, c = fmap1.shape
     rd = 2 * radius + 1
     dt = _dtype_code(fmap1)
     cdt = _dtype_code(coords)
+    md = _map_dims(fmap1, fmap2_packed, levels, map_hw)
     corr = torch.empty((b, levels, rd * rd, h, w), dtype=fmap1.dtype, device=fmap1.device)
-    nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine)
+    nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine, md)
     ws, nws = _workspace(fmap1, nbytes)
+    wsp = ws.data_ptr() if ws is not None else None
     with torch.cuda.device(fmap1.device):
-        ok = _timed("pyramid_fwd", lambda: lib.launchLocalCorrB200PyramidForward(
-            fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr.data_ptr(),
-            b, h, w, c, radius, levels, dilation, dt, cdt, bool(ymajor), float(scale), engine,
-            ws.data_ptr() if ws is not None else None, nws, _stream(fmap1)))
+        if md is None:
+            ok = _timed("pyramid_fwd", lambda: lib.launchLocalCorrB200PyramidForward(
+                fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr.data_ptr(),
+                b, h, w, c, radius, levels, dilation, dt, cdt, bool(ymajor), float(scale),
+                engine, wsp, nws, _stream(fmap1)))
+        else:
+            ok = _timed("pyramid_fwd", lambda: lib.launchLocalCorrB200PyramidForwardMapDims(
+                fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr.data_ptr(),
+                b, h, w, md[0], md[1], c, radius, levels, dilation, dt, cdt, bool(ymajor),
+                float(scale), engine, wsp, nws, _stream(fmap1)))
     _lib.check(ok, "pyramid correlation forward", lib)
     return corr
 
 
 def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels,
                           dilation=1, ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO,
-                          out=None, accumulate=0):
+                          out=None, accumulate=0, map_hw=None):
     """Returns (grad_fmap1 [B,H,W,C] dtype, grad_fmap2_packed float32).
 
     With ``out=(g1, g2)`` the gradients go into those buffers; ``accumulate``
     (flags ``_lib.ACC_FMAP1`` / ``_lib.ACC_FMAP2``) adds into them instead of
-    overwriting."""
+    overwriting. ``map_hw`` as in :func:`pyramid_corr_forward`."""
     lib = _lib.require_library()
     b, h, w, c = fmap1.shape
     dt = _dtype_code(fmap1)
     cdt = _dtype_code(coords)
+    md = _map_dims(fmap1, fmap2_packed, levels, map_hw)
     corr_grad = corr_grad.contiguous()
     if corr_grad.dtype != fmap1.dtype:
         corr_grad = corr_grad.to(fmap1.dtype)
@@ -186,14 +220,22 @@ def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels
     else:
         g1 = torch.empty_like(fmap1)
         g2 = torch.empty(fmap2_packed.shape, dtype=torch.float32, device=fmap1.device)
-    nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine)
+    nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine, md)
     ws, nws = _workspace(fmap1, nbytes)
+    wsp = ws.data_ptr() if ws is not None else None
     with torch.cuda.device(fmap1.device):
-        ok = _timed("pyramid_bwd", lambda: lib.launchLocalCorrB200PyramidBackward(
-            fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr_grad.data_ptr(),
-            g1.data_ptr(), g2.data_ptr(), b, h, w, c, radius, levels, dilation, dt, cdt,
-            bool(ymajor), float(scale), int(accumulate), engine,
-            ws.data_ptr() if ws is not None else None, nws, _stream(fmap1)))
+        if md is None:
+            ok = _timed("pyramid_bwd", lambda: lib.launchLocalCorrB200PyramidBackward(
+                fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(),
+                corr_grad.data_ptr(), g1.data_ptr(), g2.data_ptr(), b, h, w, c, radius, levels,
+                dilation, dt, cdt, bool(ymajor), float(scale), int(accumulate), engine, wsp,
+                nws, _stream(fmap1)))
+        else:
+            ok = _timed("pyramid_bwd", lambda: lib.launchLocalCorrB200PyramidBackwardMapDims(
+                fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(),
+                corr_grad.data_ptr(), g1.data_ptr(), g2.data_ptr(), b, h, w, md[0], md[1], c,
+                radius, levels, dilation, dt, cdt, bool(ymajor), float(scale),
+                int(accumulate), engine, wsp, nws, _stream(fmap1)))
     _lib.check(ok, "pyramid correlation backward", lib)
     return g1, g2
 
@@ -265,15 +307,18 @@ class PyramidBuild(torch.autograd.Function):
 
 class ScaledPyramidCorr(torch.autograd.Function):
     """scale * pyramid correlation, the fused form of the RAFT block call
-    (blocks.py:391-411: kernel launch, then reshape and division by sqrt(C))."""
+    (blocks.py:391-411: kernel launch, then reshape and division by sqrt(C)).
+    ``map_hw`` as in :func:`pyramid_corr_forward`."""
 
     @staticmethod
-    def forward(ctx, fmap1, fmap2_packed, coords, radius, levels, dilation, ymajor, scale):
+    def forward(ctx, fmap1, fmap2_packed, coords, radius, levels, dilation, ymajor, scale,
+                map_hw=None):
         coords = coords.contiguous()
         corr = pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation,
-                                    ymajor, scale)
+                                    ymajor, scale, map_hw=map_hw)
         ctx.save_for_backward(fmap1, fmap2_packed, coords)
         ctx.params = (int(radius), int(levels), int(dilation), bool(ymajor), float(scale))
+        ctx.map_hw = map_hw
         return corr
 
     @staticmethod
@@ -283,13 +328,14 @@ class ScaledPyramidCorr(torch.autograd.Function):
         g1 = g2 = None
         if ctx.needs_input_grad[0] or ctx.needs_input_grad[1]:
             g1, g2 = pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius,
-                                           levels, dilation, ymajor, scale)
+                                           levels, dilation, ymajor, scale,
+                                           map_hw=ctx.map_hw)
             if g2.dtype != fmap2_packed.dtype:
                 g2 = g2.to(fmap2_packed.dtype)
         # RAFT detaches the sampling coordinates: zeros, as the reference
         # returns (blocks.py:534-537).
         gc = torch.zeros_like(coords) if ctx.needs_input_grad[2] else None
-        return g1, g2, gc, None, None, None, None, None
+        return g1, g2, gc, None, None, None, None, None, None
 
 
 class LookupGrads:

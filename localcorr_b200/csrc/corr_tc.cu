@@ -56,7 +56,10 @@ constexpr int kColBins = kCellX;  // sort bins per cell: the level-0 base column
 constexpr int kMaxTcLevels = 4;
 constexpr int kBwd1Threads = 64 + 256 + 128;  // grad_fmap1: producer, MMA, 2 x 4 builder warps, 4 epilogue warps
 constexpr int kFwdEG = 3;          // forward epilogue warp groups
-constexpr int kFwdEpiThreads = 64 + 128 * kFwdEG;
+// forward fmap1 row gather (A tile): 4 warps, 2 at radius 8, whose
+// epilogue needs the registers of a smaller block
+constexpr int fwd_gather_warps(int radius) { return radius > 4 ? 2 : 4; }
+constexpr int fwd_threads(int radius) { return 64 + 128 * kFwdEG + 32 * fwd_gather_warps(radius); }
 
 // out[i] = v[rx + i] for rx in [0, 15], without dynamic register indexing
 // (4-stage select network on the bits of rx).
@@ -415,8 +418,10 @@ __global__ void tc_gather_rows_kernel(const __half* __restrict__ fmap1, const in
 // forward
 // ---------------------------------------------------------------------------
 template <int RADIUS>
-__global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
+__global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
   constexpr int RD = 2 * RADIUS + 1;
+  constexpr int GW = fwd_gather_warps(RADIUS);
+  constexpr int GROWS = kTile / GW / 4;  // 4-row copy groups per gather warp
   constexpr int NW = RD + 1;  // grid samples per window row
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
@@ -442,7 +447,7 @@ __global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_
   const int lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) { tc::mbar_init(full + s, 1); tc::mbar_init(empty + s, 1); }
-    tc::mbar_init(a_full, 1);
+    tc::mbar_init(a_full, 32 * GW);
     tc::mbar_init(a_empty, 1);
     for (int i = 0; i < 2; ++i) {
       tc::mbar_init(t_full + i, 1);
@@ -464,39 +469,48 @@ __global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_
   const int nwork = *p.work_count;
   volatile int* abort = &abort_flag;
 
-  if (warp == 0) {
-    // ---------------- producer ----------------
-    uint32_t gs = 0;
+  if (warp >= 2 + 4 * kFwdEG) {
+    // ---------------- A tile: the chunk's fmap1 rows ----------------
+    // 128 rows x C fp16, K-major SWIZZLE_128B, 64-channel slabs. Warp gw
+    // owns rows [gw * 128 / GW, (gw + 1) * 128 / GW); one copy instruction covers 4 rows x
+    // 128 contiguous bytes (8 lanes per row), so every request is whole
+    // 32-byte sectors. The chunk's pixel ids are loaded before the wait for
+    // the previous chunk's MMAs, and the B tiles of the chunk are requested
+    // by the TMA warp independently of this gather.
+    const int gw = warp - (2 + 4 * kFwdEG);
+    const int sub = lane & 7, rr = lane >> 3;
     int it = 0;
     for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x, ++it) {
       const int4 wk = p.work[wi];
-      const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
-      if (!tc::mbar_wait(a_empty, (it & 1) ^ 1, abort)) break;
-      // A tile: 128 rows x C fp16, K-major SWIZZLE_128B, 64-channel slabs.
-      // Lane owns rows lane + 32k; its 4 pixel ids are loaded up front so the
-      // copies do not wait on dependent index loads.
-      int rid[4];
+      const int start = wk.z, n = wk.w;
+      int rid[GROWS];
 #pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        const int t = lane + 32 * k;
-        rid[k] = t < n ? p.sorted[start + t] : -1;
+      for (int i = 0; i < GROWS; ++i) {
+        const int t = gw * 4 * GROWS + 4 * i + rr;
+        rid[i] = t < n ? p.sorted[start + t] : -1;
       }
-      for (int u = 0; u < g.KC * 8; ++u) {
-        const int kc = u >> 3, j = u & 7;
+      if (!tc::mbar_wait(a_empty, (it & 1) ^ 1, abort)) break;
+      for (int kc = 0; kc < g.KC; ++kc) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const int t = lane + 32 * k;
-          uint8_t* dst = sA + kc * 16384 + t * 128 + ((j ^ (t & 7)) << 4);
-          if (rid[k] >= 0)
-            tc::cp_async_16(dst, p.fmap1 + (long long)rid[k] * g.C + kc * 64 + j * 8, 16);
+        for (int i = 0; i < GROWS; ++i) {
+          const int t = gw * 4 * GROWS + 4 * i + rr;
+          uint8_t* dst = sA + kc * 16384 + t * 128 + ((sub ^ (t & 7)) << 4);
+          if (rid[i] >= 0)
+            tc::cp_async_16(dst, p.fmap1 + (long long)rid[i] * g.C + kc * 64 + sub * 8, 16);
           else
             tc::cp_async_16(dst, p.fmap1, 0);
         }
       }
-      tc::cp_async_wait_all();
-      tc::fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) tc::mbar_arrive(a_full);
+      tc::cp_async_mbar_arrive_noinc(a_full);
+    }
+    // Copies still in flight complete before the kernel's final barrier.
+    tc::cp_async_wait_all();
+  } else if (warp == 0) {
+    // ---------------- B tiles (TMA) ----------------
+    uint32_t gs = 0;
+    for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x) {
+      const int4 wk = p.work[wi];
+      const int b = wk.x, cell = wk.y;
       const int cy = cell / g.ncx, cx = cell - cy * g.ncx;
       const int cell_y0 = g.ylo + cy * kCellY, cell_x0 = g.xlo + cx * kCellX;
       bool ok = true;
@@ -533,6 +547,9 @@ __global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_
       bool ok = true;
       for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
         if (!tc::mbar_wait(a_full, it & 1, abort)) break;
+        // A rows arrive through cp.async completion: make their
+        // shared-memory writes visible to the tensor core's proxy.
+        tc::fence_proxy_async_smem();
         tc::tc_fence_after();
         for (int l = 0; l < g.L && ok; ++l) {
           const uint32_t idesc = tc::idesc_f16_f32(128, g.npad[l], false, false);
@@ -575,6 +592,12 @@ __global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_
     const int ge = (warp - 2) >> 2;       // epilogue group
     const int t = q * 32 + lane;          // tile row = pixel slot
     const int et = threadIdx.x - 64;      // 0..128*kFwdEG-1 for the copy
+    // copy-out walk: word i = et + k * (128 * kFwdEG) of the staged block as
+    // (row, word in row), advanced without a division per word
+    const int words = g.RDP / 2;
+    const int et_row = et / words, et_w = et - et_row * words;
+    const int step_rows = (kTile * kFwdEG) / words;
+    const int step_w = (kTile * kFwdEG) - step_rows * words;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     constexpr int NLD = (kCellX + 2 * RADIUS + 1 + 31) / 32;
     uint32_t pc = 0, ephase = 0;
@@ -655,12 +678,13 @@ __global__ void __launch_bounds__(kFwdEpiThreads, 1) tc_fwd_kernel(const __grid_
         if (!ok) break;
         // Level complete for this chunk: copy the staged rows to the scratch.
         if (!epi_sync()) { ok = false; break; }
-        const int words = g.RDP / 2;
         uint32_t* dst = reinterpret_cast<uint32_t*>(p.scratch + ((long long)l * g.npix + start) * g.RDP);
+        int row = et_row, wd2 = et_w;
         for (int i = et; i < n * words; i += kTile * kFwdEG) {
-          const int row = i / words;
-          const int wd2 = i - row * words;
           dst[i] = sOut[row * RDPS + wd2];
+          row += step_rows;
+          wd2 += step_w;
+          if (wd2 >= words) { wd2 -= words; ++row; }
         }
         if (!epi_sync()) { ok = false; break; }
       }
@@ -1645,7 +1669,7 @@ template <int RADIUS>
 bool launch_fwd_kernel(const TcFwdParams& prm, size_t smem, cudaStream_t s) {
   auto k = tc_fwd_kernel<RADIUS>;
   if (!ensure_smem_attr((const void*)k, smem)) return false;
-  k<<<num_sms(), kFwdEpiThreads, smem, s>>>(prm);
+  k<<<num_sms(), fwd_threads(RADIUS), smem, s>>>(prm);
   count_launch();
   return check_launch("tc_fwd");
 }

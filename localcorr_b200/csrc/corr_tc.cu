@@ -540,10 +540,15 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      uint32_t gs = 0, pc = 0;
+      uint32_t pc = 0;
+      int s = 0;          // B stage ring position and its fill phase
+      uint32_t ph = 0;
       int it = 0;
-      const uint32_t a_base = tc::smem_u32(sA);
-      const uint32_t b_base = tc::smem_u32(sB);
+      // descriptors: A slab kc at +kc*16 KB, B stage s at +s*stage_bytes
+      // (start-address units of 16 bytes), K steps of 32 bytes (+2)
+      const uint64_t a_desc0 = tc::smem_desc_sw128(tc::smem_u32(sA), 16, 1024);
+      const uint64_t b_desc0 = tc::smem_desc_sw128(tc::smem_u32(sB), 16, 1024);
+      const uint32_t b_stage_units = p.stage_bytes >> 4;
       bool ok = true;
       for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x, ++it) {
         if (!tc::mbar_wait(a_full, it & 1, abort)) break;
@@ -558,18 +563,16 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
             if (!tc::mbar_wait(t_empty + buf, ((pc >> 1) & 1) ^ 1, abort)) { ok = false; break; }
             tc::tc_fence_after();
             const uint32_t d = tmem + buf * 256;
-            for (int kc = 0; kc < g.KC; ++kc, ++gs) {
-              const int s = gs % NST;
-              const uint32_t use = gs / NST;
-              if (!tc::mbar_wait(full + s, use & 1, abort)) { ok = false; break; }
+            for (int kc = 0; kc < g.KC; ++kc) {
+              const int cs = s;
+              const uint32_t cph = ph;
+              if (++s == NST) { s = 0; ph ^= 1; }
+              const uint64_t ad = a_desc0 + (uint64_t)(kc * 1024);
+              const uint64_t bd = b_desc0 + (uint64_t)(cs * b_stage_units);
+              if (!tc::mbar_wait(full + cs, cph, abort)) { ok = false; break; }
               tc::tc_fence_after();
-#pragma unroll
-              for (int kk = 0; kk < 4; ++kk) {
-                const uint64_t ad = tc::smem_desc_sw128(a_base + kc * 16384 + kk * 32, 16, 1024);
-                const uint64_t bd = tc::smem_desc_sw128(b_base + s * p.stage_bytes + kk * 32, 16, 1024);
-                tc::mma_f16_ss(d, ad, bd, idesc, (kc | kk) != 0);
-              }
-              tc::mma_commit(empty + s);
+              tc::mma_f16_ss_n(d, ad, 2, bd, 2, idesc, kc != 0, 4);
+              tc::mma_commit(empty + cs);
             }
             if (!ok) break;
             tc::mma_commit(t_full + buf);
@@ -1003,9 +1006,14 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      uint32_t gs = 0;
+      int s = 0;          // stage ring position and its fill phase
+      uint32_t ph = 0;
       int it = 0;
-      const uint32_t base = tc::smem_u32(smem);
+      // descriptors: stage s at +s*SB, its B at +16 KB; K steps of 32 bytes
+      // in A (+2), of 16 rows x 128 bytes in B (+128)
+      const uint64_t a_desc0 = tc::smem_desc_sw128(tc::smem_u32(smem), 16, 1024);
+      const uint64_t b_desc0 = tc::smem_desc_sw128(tc::smem_u32(smem) + 16384, 8192, 1024);
+      const uint32_t stage_units = SB >> 4;
       const uint32_t idesc = tc::idesc_f16_f32(128, g.C, false, true);
       bool ok = true;
       int next_cell = blockIdx.x < nwork ? p.work[blockIdx.x].y : 0;
@@ -1023,24 +1031,20 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
           const int nkk = (g.UWb[l] * g.Rg[l] + 15) / 16;
           for (int gi = 0; gi < g.ngroups[l]; ++gi) {
             if (!b1_group_live(g, l, gi, m_y0, m_x0, RADIUS)) continue;
-            const int s = gs % NST;
-            const uint32_t use = gs / NST;
-            ++gs;
-            if (!tc::mbar_wait(bfull + s, use & 1, abort) ||
-                !tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
+            const int cs = s;
+            const uint32_t cph = ph;
+            if (++s == NST) { s = 0; ph ^= 1; }
+            const uint64_t ad = a_desc0 + (uint64_t)(cs * stage_units);
+            const uint64_t bd = b_desc0 + (uint64_t)(cs * stage_units);
+            if (!tc::mbar_wait(bfull + cs, cph, abort) ||
+                !tc::mbar_wait(afull + cs, cph, abort)) { ok = false; break; }
             // A rows arrive through cp.async completion: make their
             // shared-memory writes visible to the tensor core's proxy.
             tc::fence_proxy_async_smem();
             tc::tc_fence_after();
-            const uint32_t sa = base + s * SB;
-            const uint32_t sb = sa + 16384;
-            for (int kk = 0; kk < nkk; ++kk) {
-              const uint64_t ad = tc::smem_desc_sw128(sa + kk * 32, 16, 1024);
-              const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, 8192, 1024);
-              tc::mma_f16_ss(tmem + buf * 256, ad, bd, idesc, first ? 0u : 1u);
-              first = false;
-            }
-            tc::mma_commit(empty + s);
+            tc::mma_f16_ss_n(tmem + buf * 256, ad, 2, bd, 128, idesc, first ? 0u : 1u, nkk);
+            first = false;
+            tc::mma_commit(empty + cs);
           }
         }
         if (ok) tc::mma_commit(acc_full + buf);
@@ -1301,8 +1305,15 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   if (warp == 0) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      uint32_t gs = 0, ac = 0;
-      const uint32_t base = tc::smem_u32(smem);
+      uint32_t ac = 0;
+      int s = 0;          // stage ring position and its fill phase
+      uint32_t ph = 0;
+      // descriptors: stage s at +s*SB (A), its B at +2*kB2Rows*128; K steps
+      // of 16 rows x 128 bytes (+128) in both
+      const uint64_t a_desc0 = tc::smem_desc_sw128(tc::smem_u32(smem), kB2Rows * 128, 1024);
+      const uint64_t b_desc0 =
+          tc::smem_desc_sw128(tc::smem_u32(smem) + 2 * kB2Rows * 128, kB2Rows * 128, 1024);
+      const uint32_t stage_units = SB >> 4;
       const uint32_t idesc = tc::idesc_f16_f32(128, g.C, true, true);
       bool ok = true;
       for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++ac) {
@@ -1311,27 +1322,23 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         tc::tc_fence_after();
         bool first = true;
         for (;;) {
-          const int s = gs % NST;
-          const uint32_t use = gs / NST;
-          if (!tc::mbar_wait(bfull + s, use & 1, abort) ||
-              !tc::mbar_wait(afull + s, use & 1, abort)) { ok = false; break; }
+          const int cs = s;
+          const uint32_t cph = ph;
+          if (++s == NST) { s = 0; ph ^= 1; }
+          const uint64_t ad = a_desc0 + (uint64_t)(cs * stage_units);
+          const uint64_t bd = b_desc0 + (uint64_t)(cs * stage_units);
+          if (!tc::mbar_wait(bfull + cs, cph, abort) ||
+              !tc::mbar_wait(afull + cs, cph, abort)) { ok = false; break; }
           // A rows arrive through cp.async completion: make their
           // shared-memory writes visible to the tensor core's proxy.
           tc::fence_proxy_async_smem();
           tc::tc_fence_after();
-          const int flags = stage_flags[s];
-          stage_flags[s] = 0;
-          const uint32_t sa = base + s * SB;
-          const uint32_t sb = sa + 2 * kB2Rows * 128;
-#pragma unroll
-          for (int kk = 0; kk < kB2Rows / 16; ++kk) {
-            const uint64_t ad = tc::smem_desc_sw128(sa + kk * 2048, kB2Rows * 128, 1024);
-            const uint64_t bd = tc::smem_desc_sw128(sb + kk * 2048, kB2Rows * 128, 1024);
-            tc::mma_f16_ss(tmem + buf * 256, ad, bd, idesc, first ? 0u : 1u);
-            first = false;
-          }
-          tc::mma_commit(empty + s);
-          ++gs;
+          const int flags = stage_flags[cs];
+          stage_flags[cs] = 0;
+          static_assert(kB2Rows / 16 == 4, "one 4-MMA batch per stage");
+          tc::mma_f16_ss_n(tmem + buf * 256, ad, 128, bd, 128, idesc, first ? 0u : 1u, 4);
+          first = false;
+          tc::mma_commit(empty + cs);
           if (flags & 1) break;
         }
         if (!ok) break;

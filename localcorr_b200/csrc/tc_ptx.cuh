@@ -141,6 +141,49 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t adesc, uint
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z));
 }
 
+// n (1..4) MMAs into one accumulator, issued from one statement: MMA k reads
+// descriptors a0 + k*astep and b0 + k*bstep (start-address units of 16
+// bytes); the first accumulates when acc != 0, the others always. Every
+// operand is a distinct input register of the one statement: a descriptor
+// register that the next batch overwrites is not still waiting to be read
+// by a queued MMA of this batch, so batches issue back to back (one
+// descriptor per statement, rewritten per MMA, runs the MMAs at their
+// latency instead of their throughput).
+__device__ __forceinline__ void mma_f16_ss_n(uint32_t d_tmem, uint64_t a0, uint32_t astep,
+                                             uint64_t b0, uint32_t bstep, uint32_t idesc,
+                                             uint32_t acc, int n) {
+  const uint64_t a1 = a0 + astep, a2 = a1 + astep, a3 = a2 + astep;
+  const uint64_t b1 = b0 + bstep, b2 = b1 + bstep, b3 = b2 + bstep;
+  if (n >= 4) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %10, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %5, %9, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %6, %9, 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %7, %9, 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %4, %8, %9, 1;\n\t}" ::"r"(d_tmem),
+        "l"(a0), "l"(a1), "l"(a2), "l"(a3), "l"(b0), "l"(b1), "l"(b2), "l"(b3), "r"(idesc),
+        "r"(acc));
+  } else if (n == 3) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %8, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %4, %7, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %5, %7, 1;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %3, %6, %7, 1;\n\t}" ::"r"(d_tmem),
+        "l"(a0), "l"(a1), "l"(a2), "l"(b0), "l"(b1), "l"(b2), "r"(idesc), "r"(acc));
+  } else if (n == 2) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %3, %5, p;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %2, %4, %5, 1;\n\t}" ::"r"(d_tmem),
+        "l"(a0), "l"(a1), "l"(b0), "l"(b1), "r"(idesc), "r"(acc));
+  } else if (n == 1) {
+    mma_f16_ss(d_tmem, a0, b0, idesc, acc);
+  }
+}
+
 // Arrive once on `bar` when all previously issued tcgen05 ops of this thread
 // have completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {

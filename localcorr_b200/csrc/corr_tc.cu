@@ -61,21 +61,35 @@ constexpr int kFwdEG = 3;          // forward epilogue warp groups
 constexpr int fwd_gather_warps(int radius) { return radius > 4 ? 2 : 4; }
 constexpr int fwd_threads(int radius) { return 64 + 128 * kFwdEG + 32 * fwd_gather_warps(radius); }
 
-// out[i] = v[rx + i] for rx in [0, 15], without dynamic register indexing
-// (4-stage select network on the bits of rx).
+// out[i] = v[rx + i] for rx in [0, 2^SD), a select network of SD stages on
+// the bits of rx (no dynamic register indexing).
+template <int NW, int NV, int SD>
+struct WindowSelect {
+  static_assert(NV >= NW + (1 << SD) - 1, "window source too short");
+  __device__ __forceinline__ static void run(const float* v, int rx, float (&out)[NW]) {
+    constexpr int H = 1 << (SD - 1);
+    float t[NW + H - 1];
+#pragma unroll
+    for (int i = 0; i < NW + H - 1; ++i) t[i] = (rx & H) ? v[i + H] : v[i];
+    WindowSelect<NW, NW + H - 1, SD - 1>::run(t, rx, out);
+  }
+};
 template <int NW, int NV>
-__device__ __forceinline__ void window_select(const float* v, int rx, float (&out)[NW]) {
-  static_assert(NV >= NW + 15, "window source too short");
-  float a[NW + 7], b[NW + 3], c[NW + 1];
+struct WindowSelect<NW, NV, 0> {
+  __device__ __forceinline__ static void run(const float* v, int, float (&out)[NW]) {
 #pragma unroll
-  for (int i = 0; i < NW + 7; ++i) a[i] = (rx & 8) ? v[i + 8] : v[i];
-#pragma unroll
-  for (int i = 0; i < NW + 3; ++i) b[i] = (rx & 4) ? a[i + 4] : a[i];
-#pragma unroll
-  for (int i = 0; i < NW + 1; ++i) c[i] = (rx & 2) ? b[i + 2] : b[i];
-#pragma unroll
-  for (int i = 0; i < NW; ++i) out[i] = (rx & 1) ? c[i + 1] : c[i];
+    for (int i = 0; i < NW; ++i) out[i] = v[i];
+  }
+};
+
+// TMEM columns a forward window row is read in: the least of 16, 32, 64
+// holding the window (2r+2) plus the anchor offsets within a level-l cell
+// column span (16 >> l).
+__host__ __device__ constexpr int fwd_row_cols(int radius, int l) {
+  return (2 * radius + 2) + (kCellX >> l) - 1 <= 16 ? 16
+         : (2 * radius + 2) + (kCellX >> l) - 1 <= 32 ? 32 : 64;
 }
+__host__ __device__ constexpr int fwd_select_depth(int l) { return 4 - l; }
 
 struct TcGeom {
   int B, H, W, C, r, L, RD, RD2, RDP, KC, HW;
@@ -417,12 +431,54 @@ __global__ void tc_gather_rows_kernel(const __half* __restrict__ fmap1, const in
 // ---------------------------------------------------------------------------
 // forward
 // ---------------------------------------------------------------------------
+// One epilogue pass over union rows [ua, ub] of a forward part, level l
+// (select depth and TMEM read width fixed per level): the window rows of this
+// lane's pixel are picked out of each union row, bilinearly combined with the
+// previous one and the RD outputs of window row iy staged in orow.
+template <int RADIUS, int LVL>
+__device__ __forceinline__ void fwd_part_rows(uint32_t taddr, int UW, int U0, int ua, int ub,
+                                              int ry, int rx, bool valid, float wa, float wb,
+                                              float wc, float wd, bool ymajor, __half* orow) {
+  constexpr int RD = 2 * RADIUS + 1;
+  constexpr int NW = RD + 1;
+  constexpr int NC = fwd_row_cols(RADIUS, LVL);
+  float prev[NW];
+#pragma unroll
+  for (int k2 = 0; k2 < NW; ++k2) prev[k2] = 0.f;
+  for (int u = ua; u <= ub; ++u) {
+    float v[NC];
+    if constexpr (NC == 16) {
+      tc::tmem_ld16(taddr + u * UW, *reinterpret_cast<float(*)[16]>(v));
+    } else {
+#pragma unroll
+      for (int c = 0; c < NC / 32; ++c)
+        tc::tmem_ld32(taddr + u * UW + 32 * c, *reinterpret_cast<float(*)[32]>(v + 32 * c));
+    }
+    tc::tmem_ld_wait();
+    const int j = U0 + u - ry;  // window row of this grid row
+    if (valid && j >= 0 && j <= RD) {
+      float cur[NW];
+      WindowSelect<NW, NC, fwd_select_depth(LVL)>::run(v, rx, cur);
+      if (u > ua && j >= 1) {
+        const int iy = j - 1;
+        const int dbase = ymajor ? RD * iy : iy;
+        const int dstep = ymajor ? 1 : RD;
+#pragma unroll
+        for (int ix = 0; ix < RD; ++ix) {
+          const float val = wa * prev[ix] + wb * prev[ix + 1] + wc * cur[ix] + wd * cur[ix + 1];
+          orow[dbase + dstep * ix] = __float2half_rn(val);
+        }
+      }
+#pragma unroll
+      for (int k2 = 0; k2 < NW; ++k2) prev[k2] = cur[k2];
+    }
+  }
+}
+
 template <int RADIUS>
 __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __grid_constant__ TcFwdParams p) {
-  constexpr int RD = 2 * RADIUS + 1;
   constexpr int GW = fwd_gather_warps(RADIUS);
   constexpr int GROWS = kTile / GW / 4;  // 4-row copy groups per gather warp
-  constexpr int NW = RD + 1;  // grid samples per window row
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
   const TcGeom& g = p.g;
@@ -602,7 +658,6 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
     const int step_rows = (kTile * kFwdEG) / words;
     const int step_w = (kTile * kFwdEG) - step_rows * words;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    constexpr int NLD = (kCellX + 2 * RADIUS + 1 + 31) / 32;
     uint32_t pc = 0, ephase = 0;
     bool ok = true;
     auto epi_sync = [&]() -> bool {
@@ -647,34 +702,17 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
           const int rs = reff > 1 ? (reff - 2) / kFwdEG + 1 : 1;
           const int ua = ge * rs;
           const int ub = min(reff - 1, (ge + 1) * rs);
-          float prev[NW];
-#pragma unroll
-          for (int k2 = 0; k2 < NW; ++k2) prev[k2] = 0.f;
-          for (int u = ua; u <= ub; ++u) {
-            const int U = U0 + u;
-            float v[32 * NLD];
-#pragma unroll
-            for (int c = 0; c < NLD; ++c)
-              tc::tmem_ld32(lane_addr + buf * 256 + u * UW + 32 * c,
-                            *reinterpret_cast<float(*)[32]>(v + 32 * c));
-            tc::tmem_ld_wait();
-            const int j = U - ry;  // window row of this grid row
-            if (valid && j >= 0 && j <= RD) {
-              float cur[NW];
-              window_select<NW, 32 * NLD>(v, rx, cur);
-              if (u > ua && j >= 1) {
-                const int iy = j - 1;
-#pragma unroll
-                for (int ix = 0; ix < RD; ++ix) {
-                  const float val = wa * prev[ix] + wb * prev[ix + 1] + wc * cur[ix] + wd * cur[ix + 1];
-                  const int d = p.ymajor ? (ix + RD * iy) : (iy + RD * ix);
-                  orow[d] = __float2half_rn(val);
-                }
-              }
-#pragma unroll
-              for (int k2 = 0; k2 < NW; ++k2) prev[k2] = cur[k2];
-            }
-          }
+          const uint32_t taddr = lane_addr + buf * 256;
+          const bool ym = p.ymajor != 0;
+          // rx < 16 >> l: the select depth and read width of the level
+          if (l == 0)
+            fwd_part_rows<RADIUS, 0>(taddr, UW, U0, ua, ub, ry, rx, valid, wa, wb, wc, wd, ym, orow);
+          else if (l == 1)
+            fwd_part_rows<RADIUS, 1>(taddr, UW, U0, ua, ub, ry, rx, valid, wa, wb, wc, wd, ym, orow);
+          else if (l == 2)
+            fwd_part_rows<RADIUS, 2>(taddr, UW, U0, ua, ub, ry, rx, valid, wa, wb, wc, wd, ym, orow);
+          else
+            fwd_part_rows<RADIUS, 3>(taddr, UW, U0, ua, ub, ry, rx, valid, wa, wb, wc, wd, ym, orow);
           tc::tc_fence_before();
           tc::mbar_arrive(t_empty + buf);
         }

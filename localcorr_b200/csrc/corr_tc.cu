@@ -775,40 +775,28 @@ struct GintShape {
   static constexpr int RC = (16 / NU) < NG ? 16 / NU : NG;  // grid rows per staged chunk
   static constexpr int SU = (RC * NU) % 2 ? RC * NU : RC * NU + 1;  // odd unit stride
   static constexpr size_t tile_bytes = (size_t)RD * RD * 128 * 2;
-  static constexpr size_t smem_bytes = tile_bytes + (size_t)4 * 32 * SU * 16;
+  static constexpr size_t stage_bytes = (size_t)4 * 32 * SU * 16;
+  static constexpr size_t smem_bytes = tile_bytes + stage_bytes;
+  // persistent form: two 1024-aligned tiles (TMA double buffer) + staging
+  static constexpr size_t tile_pad = (tile_bytes + 1023) / 1024 * 1024;
+  static constexpr size_t tma_smem_bytes = 1024 + 2 * tile_pad + stage_bytes;
+  static constexpr bool tma_ok = RD * RD <= 256;  // one TMA box per tile
 };
 
+// One 128-pixel run (pixels pix0.., level l, image b) whose incoming
+// gradients are in `tile` ([RD*RD][128] halves): the per-pixel prologue
+// (sorted index, level base, dropped-pixel zeroing) and the records.
 template <int RADIUS>
-__global__ void __launch_bounds__(128)
-tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
-               int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
-               int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale, int ymajor,
-               int vec_ok, int acc_f1, TcGeom g) {
+__device__ __forceinline__ void gint_tile(const __half* __restrict__ tile, uint4* stage, int pix0,
+                                          int l, int b, const void* __restrict__ coords,
+                                          int coords_f32, const int* __restrict__ inv,
+                                          uint4* __restrict__ gsh, int* __restrict__ sbase,
+                                          __half* __restrict__ grad_f1, float scale, int ymajor,
+                                          int acc_f1, const TcGeom& g) {
   using S = GintShape<RADIUS>;
   constexpr int RD = S::RD, NG = S::NG, NU = S::NU, RC = S::RC, SU = S::SU;
   constexpr unsigned FULL = 0xffffffffu;
-  extern __shared__ __align__(16) uint8_t gsm[];
-  __half* tile = reinterpret_cast<__half*>(gsm);
-  const int t = threadIdx.x, warp = t >> 5, lane = t & 31;
-  uint4* stage = reinterpret_cast<uint4*>(gsm + S::tile_bytes) + warp * 32 * SU;
-  const int pix0 = blockIdx.x * 128;
-  const int l = blockIdx.y;
-  const int b = blockIdx.z;
-  const int npx = min(128, g.HW - pix0);
-  const __half* src = corr_grad + ((long long)b * g.L + l) * RD * RD * g.HW + pix0;
-  if (vec_ok && npx == 128) {
-#pragma unroll 4
-    for (int i = t; i < RD * RD * 16; i += 128) {
-      const int d = i >> 4, c = i & 15;
-      reinterpret_cast<uint4*>(tile)[i] =
-          *reinterpret_cast<const uint4*>(src + (long long)d * g.HW + c * 8);
-    }
-  } else {
-    for (int i = t; i < RD * RD * 128; i += 128) {
-      const int d = i >> 7, c = i & 127;
-      tile[i] = c < npx ? src[(long long)d * g.HW + c] : __float2half(0.f);
-    }
-  }
+  const int t = threadIdx.x, lane = t & 31;
   const int pix = pix0 + t;
   int idx = -1;
   float dx = 0.f, dy = 0.f;
@@ -841,7 +829,6 @@ tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ co
       sbase[(long long)l * g.npix + idx] = (x0 & 0xFFFF) | (y0 << 16);
     }
   }
-  __syncthreads();
   // Shift by a halves: one byte permute (odd part) and two word selects.
   const int a = (x0 - RADIUS) & 7;
   const uint32_t sel = (a & 1) ? 0x5432u : 0x7654u;
@@ -903,6 +890,109 @@ tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ co
         gsh[((long long)l * g.npix + idk) * (NG * NU) + j0 * NU + v] = stage[k * SU + v];
     }
     __syncwarp();
+  }
+}
+
+
+template <int RADIUS>
+__global__ void __launch_bounds__(128)
+tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
+               int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
+               int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale, int ymajor,
+               int vec_ok, int acc_f1, TcGeom g) {
+  using S = GintShape<RADIUS>;
+  constexpr int RD = S::RD, SU = S::SU;
+  extern __shared__ __align__(16) uint8_t gsm[];
+  __half* tile = reinterpret_cast<__half*>(gsm);
+  const int t = threadIdx.x, warp = t >> 5;
+  uint4* stage = reinterpret_cast<uint4*>(gsm + S::tile_bytes) + warp * 32 * SU;
+  const int pix0 = blockIdx.x * 128;
+  const int l = blockIdx.y;
+  const int b = blockIdx.z;
+  const int npx = min(128, g.HW - pix0);
+  const __half* src = corr_grad + ((long long)b * g.L + l) * RD * RD * g.HW + pix0;
+  if (vec_ok && npx == 128) {
+#pragma unroll 4
+    for (int i = t; i < RD * RD * 16; i += 128) {
+      const int d = i >> 4, c = i & 15;
+      reinterpret_cast<uint4*>(tile)[i] =
+          *reinterpret_cast<const uint4*>(src + (long long)d * g.HW + c * 8);
+    }
+  } else {
+    for (int i = t; i < RD * RD * 128; i += 128) {
+      const int d = i >> 7, c = i & 127;
+      tile[i] = c < npx ? src[(long long)d * g.HW + c] : __float2half(0.f);
+    }
+  }
+  __syncthreads();
+  gint_tile<RADIUS>(tile, stage, pix0, l, b, coords, coords_f32, inv, gsh, sbase, grad_f1, scale,
+                    ymajor, acc_f1, g);
+}
+
+// Persistent form for 16-byte aligned gradient rows: each block walks runs
+// blockIdx.x, +gridDim.x, ... and a TMA 2D load ([RD*RD rows][128 pixels]
+// of corr_grad viewed as [B*L*RD*RD][HW], zero past HW) brings the next
+// run's gradients in while the current one is turned into records.
+template <int RADIUS>
+__global__ void __launch_bounds__(128)
+tc_gint_tma_kernel(const __grid_constant__ CUtensorMap tmap_g, const void* __restrict__ coords,
+                   int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
+                   int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale,
+                   int ymajor, int acc_f1, int nblk, int nruns, TcGeom g) {
+  using S = GintShape<RADIUS>;
+  constexpr int RD = S::RD;
+  constexpr int SU = S::SU;
+  extern __shared__ uint8_t gsm_raw[];
+  __shared__ uint64_t full[2];
+  __shared__ int abort_flag;
+  uint8_t* gsm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gsm_raw) + 1023) & ~uintptr_t(1023));
+  const int t = threadIdx.x, warp = t >> 5;
+  uint4* stage = reinterpret_cast<uint4*>(gsm + 2 * S::tile_pad) + warp * 32 * SU;
+  if (t == 0) {
+    tc::mbar_init(full, 1);
+    tc::mbar_init(full + 1, 1);
+    tc::fence_mbar_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  volatile int* abort = &abort_flag;
+  // run k: pixel block k % nblk of (image, level) = k / nblk (image major)
+  auto issue = [&](int k, int buf) {
+    const int bl = k / nblk;
+    const int pb = k - bl * nblk;
+    const int b = bl / g.L, l = bl - b * g.L;
+    tc::fence_proxy_async_smem();
+    tc::mbar_arrive_expect_tx(full + buf, (uint32_t)S::tile_bytes);
+    tc::tma_load_2d(gsm + buf * S::tile_pad, &tmap_g, full + buf, pb * 128,
+                    (b * g.L + l) * RD * RD);
+  };
+  if (t == 0 && (int)blockIdx.x < nruns) issue(blockIdx.x, 0);
+  int i = 0;
+  bool pending_next = false;
+  for (int k = blockIdx.x; k < nruns; k += gridDim.x, ++i) {
+    const int buf = i & 1;
+    const int kn = k + gridDim.x;
+    // the other buffer was last read by run i-1, which every thread
+    // finished before the barrier that ended iteration i-1
+    pending_next = kn < nruns;
+    if (t == 0 && pending_next) issue(kn, buf ^ 1);
+    if (!tc::mbar_wait(full + buf, (i >> 1) & 1, abort)) break;
+    const int bl = k / nblk;
+    const int pb = k - bl * nblk;
+    const int b = bl / g.L, l = bl - b * g.L;
+    gint_tile<RADIUS>(reinterpret_cast<const __half*>(gsm + buf * S::tile_pad), stage, pb * 128,
+                      l, b, coords, coords_f32, inv, gsh, sbase, grad_f1, scale, ymajor, acc_f1,
+                      g);
+    __syncthreads();
+    pending_next = false;
+  }
+  if (abort_flag) {
+    // copies still in flight land before the block's shared memory goes
+    if (t == 0) {
+      tc::mbar_wait_drain(full + (i & 1), (i >> 1) & 1);
+      if (pending_next) tc::mbar_wait_drain(full + ((i + 1) & 1), ((i + 1) >> 1) & 1);
+      atomicExch(&g_tc_status, 1);
+    }
   }
 }
 
@@ -1845,16 +1935,44 @@ template <int RADIUS>
 bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __half* corr_grad,
                         const int* inv, uint4* gsh, float scale, int ymajor, cudaStream_t s) {
   const TcGeom& g = p1.g;
-  dim3 ug((g.HW + 127) / 128, g.L, g.B);
-  auto k0 = tc_gint_kernel<RADIUS>;
-  const size_t smem0 = GintShape<RADIUS>::smem_bytes;
-  if (!ensure_smem_attr((const void*)k0, smem0)) return false;
-  // 16-byte loads of the incoming gradient rows need HW % 8 == 0 and an
-  // aligned base
+  using GS = GintShape<RADIUS>;
+  // 16-byte loads (and TMA rows) of the incoming gradient need HW % 8 == 0
+  // and an aligned base
   const int vec_ok = (g.HW % 8 == 0) && (reinterpret_cast<uintptr_t>(corr_grad) % 16 == 0);
-  k0<<<ug, 128, smem0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gsh,
-                            const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, vec_ok,
-                            p1.acc_f1, g);
+  auto encode = get_encode_fn();
+  CUtensorMap gmap;
+  bool tma = false;
+  if (vec_ok && GS::tma_ok && encode) {
+    // corr_grad as [B*L*RD*RD rows][HW], boxes of RD*RD rows x 128 pixels
+    cuuint64_t dims[2] = {(cuuint64_t)g.HW, (cuuint64_t)g.B * g.L * g.RD2};
+    cuuint64_t strides[1] = {(cuuint64_t)g.HW * 2};
+    cuuint32_t box[2] = {128, (cuuint32_t)g.RD2};
+    cuuint32_t estr[2] = {1, 1};
+    tma = encode(&gmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void*)corr_grad, dims, strides, box,
+                 estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  }
+  if (tma) {
+    auto k0 = tc_gint_tma_kernel<RADIUS>;
+    const size_t smem0 = GS::tma_smem_bytes;
+    if (!ensure_smem_attr((const void*)k0, smem0)) return false;
+    const int nblk = (g.HW + 127) / 128;
+    const int nruns = nblk * g.L * g.B;
+    const int per_sm = std::max(1, (int)((size_t)max_dyn_smem() / (smem0 + 1024)));
+    const int grid = std::min(nruns, num_sms() * per_sm);
+    k0<<<grid, 128, smem0, s>>>(gmap, p1.coords, p1.coords_f32, inv, gsh,
+                                const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, p1.acc_f1,
+                                nblk, nruns, g);
+  } else {
+    dim3 ug((g.HW + 127) / 128, g.L, g.B);
+    auto k0 = tc_gint_kernel<RADIUS>;
+    const size_t smem0 = GS::smem_bytes;
+    if (!ensure_smem_attr((const void*)k0, smem0)) return false;
+    k0<<<ug, 128, smem0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gsh,
+                              const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, vec_ok,
+                              p1.acc_f1, g);
+  }
   count_launch();
   if (!check_launch("tc_gint")) return false;
   const size_t smem1 = 1024 + (size_t)p1.nstage * p1.stage_bytes + 256;

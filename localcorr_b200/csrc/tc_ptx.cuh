@@ -47,6 +47,18 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for the phase of parity `parity` to complete, for at most
+// `timeout_ns`, regardless of any abort flag (draining copies in flight
+// before a block exits). Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity,
+                                                uint64_t timeout_ns = 2000000000ull) {
+  const uint64_t t0 = globaltimer();
+  for (uint32_t i = 0;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63) == 63 && globaltimer() - t0 > timeout_ns) return false;
+  }
+}
+
+// Wait for the phase of parity `parity` to complete, for at most
 // `timeout_ns`. Gives up early when *abort is set by another thread. On
 // timeout, sets *abort and returns false; every caller then winds down.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,

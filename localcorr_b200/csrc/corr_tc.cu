@@ -244,144 +244,100 @@ __global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ 
   keyrank[gid] = kr;
 }
 
-// One CTA: exclusive scan over the cells of the per-cell counts (a cell's
-// count is the sum of its column bins) and of the per-cell chunk counts
-// (work-list offsets). Pass 1 reads every cell's bins (coalesced) into a
-// shared (count, chunks) array; each thread then scans a run of
-// consecutive cells in place and one block scan places the runs; pass 2
-// writes the offsets of every (cell, column) bin into the sorted order
-// (bins in order, so a cell's pixels are sorted by their base column), the
-// work list {b, cell, first sorted index, pixel count <= 128}, and the
-// number of sorted pixels after the last bin.
-constexpr int kScanSmemCells = 24576;  // shared (count, chunks) pairs: 192 KB
-__global__ void __launch_bounds__(1024)
-tc_scan_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
-               int4* __restrict__ work, int* __restrict__ work_count, int ncell_total,
-               int ncell) {
-  using Scan = cub::BlockScan<int2, 1024>;
-  __shared__ typename Scan::TempStorage tmp;
-  extern __shared__ int2 cs[];
-  auto cell_bins = [&](int i, int* bins) {
-    const int4* src = reinterpret_cast<const int4*>(counts + (long long)i * kColBins);
+// Scan of the sort bins, three passes over the cells (all blocks busy
+// instead of one): per-cell totals (pixels; 128-pixel chunks = work
+// entries) scanned within blocks of kScanBlock cells, the block totals
+// scanned, then every (cell, column) bin offset into the sorted order (bins
+// in order, so a cell's pixels are sorted by their base column), a final
+// entry = number of sorted pixels, and the work list
+// {b, cell, first sorted index, pixel count <= 128}.
+constexpr int kScanBlock = 256;
+struct PairSum {
+  __device__ int2 operator()(int2 a, int2 b) const { return make_int2(a.x + b.x, a.y + b.y); }
+};
+
+__device__ __forceinline__ void load_cell_bins(const int* __restrict__ counts, int i,
+                                               int (&bins)[kColBins]) {
+  const int4* src = reinterpret_cast<const int4*>(counts + (long long)i * kColBins);
 #pragma unroll
-    for (int q = 0; q < kColBins / 4; ++q) {
-      const int4 v = src[q];
-      bins[4 * q] = v.x; bins[4 * q + 1] = v.y; bins[4 * q + 2] = v.z; bins[4 * q + 3] = v.w;
-    }
-  };
-  for (int i = threadIdx.x; i < ncell_total; i += blockDim.x) {
-    int bins[kColBins];
-    cell_bins(i, bins);
-    int cnt = 0;
-#pragma unroll
-    for (int q = 0; q < kColBins; ++q) cnt += bins[q];
-    cs[i] = make_int2(cnt, (cnt + kTile - 1) / kTile);
-  }
-  __syncthreads();
-  const int cpt = (ncell_total + 1023) / 1024;
-  const int c0 = min((int)threadIdx.x * cpt, ncell_total), c1 = min(c0 + cpt, ncell_total);
-  int2 run = make_int2(0, 0);
-  for (int i = c0; i < c1; ++i) { run.x += cs[i].x; run.y += cs[i].y; }
-  int2 ex, tot;
-  struct Pair { __device__ int2 operator()(int2 a, int2 b) const { return make_int2(a.x + b.x, a.y + b.y); } };
-  Scan(tmp).ExclusiveScan(run, ex, make_int2(0, 0), Pair(), tot);
-  for (int i = c0; i < c1; ++i) {
-    const int2 v = cs[i];
-    cs[i] = ex;
-    ex.x += v.x;
-    ex.y += v.y;
-  }
-  __syncthreads();
-  for (int i = threadIdx.x; i < ncell_total; i += blockDim.x) {
-    int bins[kColBins];
-    cell_bins(i, bins);
-    const int off = cs[i].x, coff = cs[i].y;
-    int acc = off;
-    int4* dst = reinterpret_cast<int4*>(offsets + (long long)i * kColBins);
-#pragma unroll
-    for (int q = 0; q < kColBins / 4; ++q) {
-      int4 v;
-      v.x = acc; acc += bins[4 * q];
-      v.y = acc; acc += bins[4 * q + 1];
-      v.z = acc; acc += bins[4 * q + 2];
-      v.w = acc; acc += bins[4 * q + 3];
-      dst[q] = v;
-    }
-    const int cnt = acc - off;
-    const int nch = (cnt + kTile - 1) / kTile;
-    const int b = i / ncell;
-    const int cell = i - b * ncell;
-    for (int j = 0; j < nch; ++j)
-      work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
-  }
-  if (threadIdx.x == 0) {
-    *work_count = tot.y;
-    offsets[(long long)ncell_total * kColBins] = tot.x;
+  for (int q = 0; q < kColBins / 4; ++q) {
+    const int4 v = src[q];
+    bins[4 * q] = v.x; bins[4 * q + 1] = v.y; bins[4 * q + 2] = v.z; bins[4 * q + 3] = v.w;
   }
 }
 
-// Fallback for more cells than the shared-memory scan holds.
-// One CTA: exclusive scan over the cells of the per-cell counts (a cell's
-// count is the sum of its column bins) and of the per-cell chunk counts
-// (work-list offsets); writes the offsets of every (cell, column) bin into
-// the sorted order (bins in order, so a cell's pixels are sorted by their
-// base column), a final entry = number of sorted pixels, and the work list:
-// {b, cell, first sorted index, pixel count <= 128}.
+__global__ void __launch_bounds__(kScanBlock)
+tc_cellscan_kernel(const int* __restrict__ counts, int2* __restrict__ cellpre,
+                   int2* __restrict__ bsum, int ncell_total) {
+  using Scan = cub::BlockScan<int2, kScanBlock>;
+  __shared__ typename Scan::TempStorage tmp;
+  const int i = blockIdx.x * kScanBlock + threadIdx.x;
+  int cnt = 0;
+  if (i < ncell_total) {
+    int bins[kColBins];
+    load_cell_bins(counts, i, bins);
+#pragma unroll
+    for (int q = 0; q < kColBins; ++q) cnt += bins[q];
+  }
+  int2 ex, tot;
+  Scan(tmp).ExclusiveScan(make_int2(cnt, (cnt + kTile - 1) / kTile), ex, make_int2(0, 0),
+                          PairSum(), tot);
+  if (i < ncell_total) cellpre[i] = ex;
+  if (threadIdx.x == 0) bsum[blockIdx.x] = tot;
+}
+
 __global__ void __launch_bounds__(1024)
-tc_scan_big_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
-               int4* __restrict__ work, int* __restrict__ work_count, int ncell_total,
-               int ncell) {
+tc_blockscan_kernel(int2* __restrict__ bsum, int nblocks, int* __restrict__ total,
+                    int* __restrict__ work_count) {
   using Scan = cub::BlockScan<int2, 1024>;
   __shared__ typename Scan::TempStorage tmp;
-  __shared__ int carry[2];
-  if (threadIdx.x == 0) { carry[0] = 0; carry[1] = 0; }
+  __shared__ int2 carry;
+  if (threadIdx.x == 0) carry = make_int2(0, 0);
   __syncthreads();
-  for (int base = 0; base < ncell_total; base += 1024) {
+  for (int base = 0; base < nblocks; base += 1024) {
     const int i = base + threadIdx.x;
-    int bins[kColBins];
-    int cnt = 0;
-    if (i < ncell_total) {
-      const int4* src = reinterpret_cast<const int4*>(counts + (long long)i * kColBins);
-#pragma unroll
-      for (int q = 0; q < kColBins / 4; ++q) {
-        const int4 v = src[q];
-        bins[4 * q] = v.x; bins[4 * q + 1] = v.y; bins[4 * q + 2] = v.z; bins[4 * q + 3] = v.w;
-      }
-#pragma unroll
-      for (int q = 0; q < kColBins; ++q) cnt += bins[q];
-    }
-    const int nch = (cnt + kTile - 1) / kTile;
-    int2 in = make_int2(cnt, nch), ex, tot;
-    // Scan both values with a pair-sum operator.
-    struct Pair { __device__ int2 operator()(int2 a, int2 b) const { return make_int2(a.x + b.x, a.y + b.y); } };
-    Scan(tmp).ExclusiveScan(in, ex, make_int2(0, 0), Pair(), tot);
-    const int off = carry[0] + ex.x;
-    const int coff = carry[1] + ex.y;
-    if (i < ncell_total) {
-      int run = off;
-      int4* dst = reinterpret_cast<int4*>(offsets + (long long)i * kColBins);
-#pragma unroll
-      for (int q = 0; q < kColBins / 4; ++q) {
-        int4 v;
-        v.x = run; run += bins[4 * q];
-        v.y = run; run += bins[4 * q + 1];
-        v.z = run; run += bins[4 * q + 2];
-        v.w = run; run += bins[4 * q + 3];
-        dst[q] = v;
-      }
-      const int b = i / ncell;
-      const int cell = i - b * ncell;
-      for (int j = 0; j < nch; ++j)
-        work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
-    }
+    const int2 v = i < nblocks ? bsum[i] : make_int2(0, 0);
+    int2 ex, tot;
+    Scan(tmp).ExclusiveScan(v, ex, make_int2(0, 0), PairSum(), tot);
+    const int2 c = carry;
+    if (i < nblocks) bsum[i] = make_int2(c.x + ex.x, c.y + ex.y);
     __syncthreads();
-    if (threadIdx.x == 0) { carry[0] += tot.x; carry[1] += tot.y; }
+    if (threadIdx.x == 0) carry = make_int2(c.x + tot.x, c.y + tot.y);
     __syncthreads();
   }
   if (threadIdx.x == 0) {
-    *work_count = carry[1];
-    offsets[(long long)ncell_total * kColBins] = carry[0];
+    *total = carry.x;
+    *work_count = carry.y;
   }
+}
+
+__global__ void __launch_bounds__(kScanBlock)
+tc_cellwrite_kernel(const int* __restrict__ counts, const int2* __restrict__ cellpre,
+                    const int2* __restrict__ bsum, int* __restrict__ offsets,
+                    int4* __restrict__ work, int ncell_total, int ncell) {
+  const int i = blockIdx.x * kScanBlock + threadIdx.x;
+  if (i >= ncell_total) return;
+  int bins[kColBins];
+  load_cell_bins(counts, i, bins);
+  const int2 pre = cellpre[i], bo = bsum[blockIdx.x];
+  const int off = bo.x + pre.x, coff = bo.y + pre.y;
+  int acc = off;
+  int4* dst = reinterpret_cast<int4*>(offsets + (long long)i * kColBins);
+#pragma unroll
+  for (int q = 0; q < kColBins / 4; ++q) {
+    int4 v;
+    v.x = acc; acc += bins[4 * q];
+    v.y = acc; acc += bins[4 * q + 1];
+    v.z = acc; acc += bins[4 * q + 2];
+    v.w = acc; acc += bins[4 * q + 3];
+    dst[q] = v;
+  }
+  const int cnt = acc - off;
+  const int nch = (cnt + kTile - 1) / kTile;
+  const int b = i / ncell;
+  const int cell = i - b * ncell;
+  for (int j = 0; j < nch; ++j)
+    work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
 }
 
 __global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* __restrict__ offsets,
@@ -1677,7 +1633,8 @@ int num_sms() {
 }
 
 struct WsLayout {
-  size_t counts, offsets, keyrank, sorted, inv, work, work_count, sbase, scratch, gsh, f1s;
+  size_t counts, offsets, keyrank, sorted, inv, work, work_count, cellpre, bsum, sbase, scratch,
+      gsh, f1s;
   size_t fwd_total, total;  // bytes the forward / the backward need
   long long max_work;
 };
@@ -1696,6 +1653,8 @@ WsLayout ws_layout(const TcGeom& g) {
   w.inv = o; o = align256(o + (size_t)g.npix * 4);
   w.work = o; o = align256(o + (size_t)w.max_work * 16);
   w.work_count = o; o = align256(o + 4);
+  w.cellpre = o; o = align256(o + ncells * 8);
+  w.bsum = o; o = align256(o + (ncells + kScanBlock - 1) / kScanBlock * 8);
   w.sbase = o; o = align256(o + (size_t)g.L * g.npix * 4);
   w.scratch = o; o = align256(o + (size_t)g.L * g.npix * g.RDP * 2);
   w.fwd_total = o;
@@ -1714,6 +1673,8 @@ struct TcWs {
   int* inv;
   int4* work;
   int* work_count;
+  int2* cellpre;
+  int2* bsum;
   int* sbase;
   __half* scratch;
   uint4* gsh;
@@ -1730,6 +1691,8 @@ TcWs ws_pointers(void* ws, const WsLayout& L) {
   p.inv = reinterpret_cast<int*>(w + L.inv);
   p.work = reinterpret_cast<int4*>(w + L.work);
   p.work_count = reinterpret_cast<int*>(w + L.work_count);
+  p.cellpre = reinterpret_cast<int2*>(w + L.cellpre);
+  p.bsum = reinterpret_cast<int2*>(w + L.bsum);
   p.sbase = reinterpret_cast<int*>(w + L.sbase);
   p.scratch = reinterpret_cast<__half*>(w + L.scratch);
   p.gsh = reinterpret_cast<uint4*>(w + L.gsh);
@@ -1750,17 +1713,18 @@ bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStr
   count_launch();
   if (!check_launch("tc_hist")) return false;
   const int ncells = g.B * g.ncell;
-  if (ncells <= kScanSmemCells) {
-    const size_t smem = (size_t)ncells * sizeof(int2);
-    if (!ensure_smem_attr((const void*)tc_scan_kernel, smem)) return false;
-    tc_scan_kernel<<<1, 1024, smem, s>>>(W.counts, W.offsets, W.work, W.work_count, ncells,
-                                         g.ncell);
-  } else {
-    tc_scan_big_kernel<<<1, 1024, 0, s>>>(W.counts, W.offsets, W.work, W.work_count, ncells,
-                                          g.ncell);
-  }
+  const int nsb = (ncells + kScanBlock - 1) / kScanBlock;
+  tc_cellscan_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, ncells);
   count_launch();
-  if (!check_launch("tc_scan")) return false;
+  if (!check_launch("tc_cellscan")) return false;
+  tc_blockscan_kernel<<<1, 1024, 0, s>>>(W.bsum, nsb, W.offsets + (size_t)ncells * kColBins,
+                                         W.work_count);
+  count_launch();
+  if (!check_launch("tc_blockscan")) return false;
+  tc_cellwrite_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, W.offsets,
+                                                 W.work, ncells, g.ncell);
+  count_launch();
+  if (!check_launch("tc_cellwrite")) return false;
   tc_scatter_kernel<<<blocks, threads, 0, s>>>(W.keyrank, W.offsets, W.sorted, W.inv, g);
   count_launch();
   return check_launch("tc_scatter");

@@ -287,26 +287,30 @@ def timed_loop(fn, steps, device):
 
 def cpu_baseline_sample(cfg, seconds_hint=20.0):
     """Time the reference CPU formulation (restated in oracle/oracle.py) on a
-    bounded sample: one image, a band of fmap1 rows, fwd + bwd, float32."""
+    bounded sample: one image, a band of fmap1 rows, float32; forward and
+    backward, or forward only for the forward-only workloads."""
     from oracle import oracle
 
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     c, h, w, L, r = cfg["C"], cfg["H"], cfg["W"], cfg["L"], cfg["r"]
+    bwd = bool(cfg["backward"])
     rows = max(1, min(h, 32))
     f1, f2 = oracle.make_fmaps(1, c, h, w, seed=5)
     co = oracle.make_coords_gauss_oob(1, h, w, 6.0, 0.05, seed=6)
-    f1 = f1[:, :, :rows].contiguous().requires_grad_(True)
-    f2 = f2.clone().requires_grad_(True)
+    f1 = f1[:, :, :rows].contiguous().requires_grad_(bwd)
+    f2 = f2.clone().requires_grad_(bwd)
     co = co[:, :, :rows].contiguous()
     t0 = time.perf_counter()
-    out = oracle.pyramid_corr_matmul(f1, f2, co, L, r) / math.sqrt(c)
-    out.backward(torch.ones_like(out))
+    with torch.set_grad_enabled(bwd):
+        out = oracle.pyramid_corr_matmul(f1, f2, co, L, r) / math.sqrt(c)
+        if bwd:
+            out.backward(torch.ones_like(out))
     dt = time.perf_counter() - t0
     n = rows * w * L * (2 * r + 1) ** 2
     return {"value": n / dt / 1e9, "unit": "Glookups/s", "cores": threads, "kind": "port",
             "sample": f"1 image, {rows} of {h} fmap1 rows x {w} cols, C={c}, L={L}, r={r}, "
-                      "fp32, fwd+bwd, oracle/oracle.py:pyramid_corr_matmul",
+                      f"fp32, {'fwd+bwd' if bwd else 'fwd'}, oracle/oracle.py:pyramid_corr_matmul",
             "seconds": dt}
 
 

@@ -119,3 +119,30 @@ def test_spatial_validation(lib):
     assert ok is False
     ok = lib.launchLocalCorrB200SpatialForward(None, None, None, 0, 4, 8, 8, 4, 1, 0, 1.0, None)
     assert ok is True
+
+
+def test_map_dims_launchers_validate_the_map_size(lib):
+    # the map's levels must be non-empty: a 4-row map has no level 3
+    ok = lib.launchLocalCorrB200PyramidForwardMapDims(None, None, None, None, 1, 16, 16, 4, 64,
+                                                      8, 2, 4, 1, 0, 0, False, 1.0, 0, None, 0,
+                                                      None)
+    assert ok is False and "empty" in _lib.last_error(lib)
+    ok = lib.launchLocalCorrB200PyramidBackwardMapDims(None, None, None, None, None, None, 1, 16,
+                                                       16, 64, 4, 8, 2, 4, 1, 0, 0, False, 1.0, 0,
+                                                       0, None, 0, None)
+    assert ok is False and "empty" in _lib.last_error(lib)
+    # an empty pixel band is a successful no-op whatever the map
+    ok = lib.launchLocalCorrB200PyramidForwardMapDims(None, None, None, None, 1, 0, 16, 64, 64, 8,
+                                                      2, 4, 1, 0, 0, False, 1.0, 0, None, 0,
+                                                      None)
+    assert ok is True
+    assert lib.localCorrB200PyramidWorkspaceBytesMapDims(1, 16, 16, 4, 64, 8, 2, 4, 1, 0, 0) == 0
+
+
+def test_map_dims_prototypes_extend_the_plain_ones():
+    fwd = _lib.PROTOTYPES["launchLocalCorrB200PyramidForward"][1]
+    fwd2 = _lib.PROTOTYPES["launchLocalCorrB200PyramidForwardMapDims"][1]
+    assert fwd2[:7] == fwd[:7] and fwd2[7:9] == [ctypes.c_int] * 2 and fwd2[9:] == fwd[7:]
+    bwd = _lib.PROTOTYPES["launchLocalCorrB200PyramidBackward"][1]
+    bwd2 = _lib.PROTOTYPES["launchLocalCorrB200PyramidBackwardMapDims"][1]
+    assert bwd2[:9] == bwd[:9] and bwd2[9:11] == [ctypes.c_int] * 2 and bwd2[11:] == bwd[9:]

@@ -1,13 +1,17 @@
 """Benchmark of the localcorr hot path (RAFT pyramid correlation, fwd+bwd).
 
 Contract: ``python bench.py --gpus N --steps K --warmup W [--impl ours|reference]``
-prints ONE JSON line on rank 0. Under torchrun (N>1) every rank runs the
-same per-GPU workload on its own batch shard with no collective in the data
-path (weak scaling); the timed region is bracketed by a barrier and a device
-synchronisation on both sides and the elapsed time is the max over ranks.
+prints ONE JSON line on rank 0. Under torchrun (N>1) each rank runs its
+shard of the workload with no collective in the data path (row-band
+workloads: one all-gather per frame); the timed region is bracketed by a
+barrier and a device synchronisation on both sides and the elapsed time is
+the max over ranks.
 
 Workload (default, benchmark configuration 2): RAFT 1/8-resolution training
-correlation, float16, B=8 per GPU, C=256, 135x240, 4 levels, radius 4.
+correlation, float16, a global batch of B=8 split over the N GPUs (8/N images
+per rank: strong scaling, as the configuration is defined), C=256, 135x240,
+4 levels, radius 4. ``raft_train_1080p_weak`` runs B=8 on every GPU instead
+(weak scaling).
 fmap1/fmap2 ~ N(0,1) (the 1/sqrt(C) is the block's output scale), coords =
 grid + N(0, 6^2) flow with 5% of the pixels pushed out of bounds, 12 lookups
 per step with coords perturbed by N(0,1) each. One step = block build (NHWC
@@ -49,8 +53,12 @@ import torch  # noqa: E402
 
 CONFIGS = {
     # name: (B per GPU, C, H, W, levels, radius, lookups per step, dtype)
+    # global batch 8 split over the ranks (strong scaling)
     "raft_train_1080p": dict(B=8, C=256, H=135, W=240, L=4, r=4, iters=12, dtype="f16",
-                             coords="gauss_oob", fdist="normal", backward=True),
+                             coords="gauss_oob", fdist="normal", backward=True, split=True),
+    # B=8 on every rank (weak scaling)
+    "raft_train_1080p_weak": dict(B=8, C=256, H=135, W=240, L=4, r=4, iters=12, dtype="f16",
+                                  coords="gauss_oob", fdist="normal", backward=True),
     "raft_cpu_case": dict(B=1, C=256, H=46, W=62, L=4, r=4, iters=1, dtype="f32",
                           coords="uniform8", fdist="normal", backward=True),
     "raft_4k_inference": dict(B=1, C=256, H=270, W=480, L=4, r=4, iters=24, dtype="f16",
@@ -199,14 +207,17 @@ class ClockSampler:
 
 
 def make_inputs(cfg, rank, device):
-    """Seeded synthetic inputs of one rank: its own batch shard, or (row-band
-    workloads, cfg["band"] = (y0, y1)) its rows of the one frame all ranks share."""
+    """Seeded synthetic inputs of one rank: its own batch shard (weak
+    scaling), its slice [rank*B, (rank+1)*B) of the one global batch all ranks
+    share (cfg["split"], strong scaling), or (row-band workloads,
+    cfg["band"] = (y0, y1)) its rows of the one frame all ranks share."""
     from oracle import oracle
 
-    seed = 0 if cfg.get("bands") else rank
+    shared = cfg.get("bands") or cfg.get("split")
+    seed = 0 if shared else rank
     g = torch.Generator().manual_seed(1234 + seed)
     dt = torch.float16 if cfg["dtype"] == "f16" else torch.float32
-    b, c, h, w = cfg["B"], cfg["C"], cfg["H"], cfg["W"]
+    b, c, h, w = cfg.get("global_B", cfg["B"]), cfg["C"], cfg["H"], cfg["W"]
     f1, f2 = oracle.make_fmaps(b, c, h, w, seed=1234 + seed, dist=cfg["fdist"])
     kind = cfg["coords"]
     if kind == "gauss_oob":
@@ -234,6 +245,13 @@ def make_inputs(cfg, rank, device):
     if cfg["backward"]:
         grads = [torch.randn(b, cfg["L"] * rd * rd, h, w, generator=g).to(dt)
                  for _ in range(cfg["iters"])]
+    if cfg.get("split"):
+        lo, hi = rank * cfg["B"], (rank + 1) * cfg["B"]
+        f1 = f1[lo:hi].contiguous()
+        f2 = f2[lo:hi].contiguous()
+        coords = [co[lo:hi].contiguous() for co in coords]
+        if grads is not None:
+            grads = [gg[lo:hi].contiguous() for gg in grads]
     pin = (lambda t: t.pin_memory()) if torch.cuda.is_available() else (lambda t: t)
     host = dict(
         f1=pin(f1.to(dt)), f2=pin(f2.to(dt)),
@@ -360,6 +378,12 @@ def main(argv=None):
         return reference_arm(args, cfg, args.config)
 
     rank, local_rank, world = _env_rank()
+    if cfg.get("split"):
+        if cfg["B"] % world:
+            raise SystemExit(f"{args.config}: the global batch {cfg['B']} does not split over "
+                             f"{world} ranks")
+        cfg["global_B"] = cfg["B"]
+        cfg["B"] = cfg["B"] // world
     if cfg.get("bands"):
         from localcorr_b200 import bands
 
@@ -506,7 +530,8 @@ def main(argv=None):
             "metric": metric_name(cfg), "value": value, "unit": "Glookups/s", "n_gpus": world,
             "steps": args.steps, "warmup": max(3, args.warmup),
             "ms_per_step": 1e3 * elapsed / args.steps, "higher_is_better": True,
-            "scaling": "strong" if cfg.get("bands") else "weak", "vs_baseline": None,
+            "scaling": "strong" if (cfg.get("bands") or cfg.get("split")) else "weak",
+            "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic",
             "config": {"workload": args.config, "B_per_gpu": cfg["B"], "global_batch":
                        cfg["B"] * shards, "C": cfg["C"], "H": cfg["H"], "W": cfg["W"],
@@ -514,11 +539,16 @@ def main(argv=None):
                        cfg["iters"], "backward": cfg["backward"],
                        "parallelism": (f"row-band x{world}: one all-gather of the band "
                                        "pyramids per frame" if cfg.get("bands") else
+                                       f"batch-split x{world}: {cfg['B']} of the global "
+                                       f"{cfg['B'] * shards} images per rank, no collective"
+                                       if cfg.get("split") else
                                        f"batch-shard x{world}, no collective"),
                        "l2": "inputs larger than L2 (no flush)"},
             "e2e": {"value": e2e_value, "unit": "Glookups/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 8,
-                    "note": "inputs of step i+1 copied on a second stream during step i"},
+                    "note": "inputs of step i+1 copied on a second stream during step i; "
+                            "the read-back is a float64 checksum of the step's gradients "
+                            "(they stay on the device, as in a training loop)"},
             "gpu_launches": launches,
             "roofline": roof,
             "cpu_baseline": cpu,

@@ -58,7 +58,10 @@ extern "C" {
 /* Replaces launchLocalCorrCudaPyramidForward,
  * cuda_pyramid/localcorr_cuda_pyramid_kernel.h:39-53. isHalf selects float16
  * for every pointer. Scratch, when the tensor-core engine needs it, comes from
- * a per-device cache owned by the library (stream-ordered, grown on demand). */
+ * one buffer per device owned by the library (grown on demand with
+ * cudaMallocAsync/cudaFreeAsync); a call on another stream than the previous
+ * call first waits, on the GPU, for that call's kernels (an event), so calls
+ * from several streams or threads are safe and run one after the other. */
 LCB200_API bool launchLocalCorrCudaPyramidForward(
     const void* fmap1, const void* fmap2_packed, const void* coords, void* corr,
     int B, int H1, int W1, int C, int radius, int levels, int dilation,
@@ -154,8 +157,10 @@ LCB200_API bool launchLocalCorrB200PyramidBackwardMapDims(
  *    C in {64,128,192,256}, radius in {3,4,8}; coords float16 or float32.
  *  - Problems whose scratch (localCorrB200PyramidWorkspaceBytes) exceeds
  *    LCB200_NOALLOC_SCRATCH_BYTES are rejected (false, message says so).
- *  - The first call on a device looks up the array's device address; make
- *    that first call before any stream capture.
+ *  - Every call looks up the array's device address on the current device
+ *    (cudaGetSymbolAddress, no allocation); the first call on a device may
+ *    also load the library's device code, so make that first call before
+ *    any stream capture.
  *  - All calls on a device share the one array: calls that can overlap on
  *    the GPU (different streams, no ordering) race and must be serialised by
  *    the caller. Each call starts from a cleared state (no carry-over). */

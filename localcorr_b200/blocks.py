@@ -106,8 +106,8 @@ class LocalCorrCudaPyramidSpatialOnnx(torch.autograd.Function):
             bsz = f1s[0]
         else:
             raise RuntimeError(
-                "Could not infer the batch size of the LocalCorrCudaPyramid ONNX node: both "
-                "fmap1 and fmap2 have unknown static shapes.")
+                "spatial plugin-node export packs fmap2 per image and so needs a static "
+                "batch dimension on fmap1 or fmap2; the traced graph has no shape for either")
         packed = g.op("Reshape", fmap2,
                       g.op("Constant", value_t=torch.tensor([bsz, -1], dtype=torch.int64)))
         node = g.op("custom_ops::LocalCorrCudaPyramid", fmap1, packed, coords,

@@ -137,37 +137,83 @@ bool validate_pyramid(int B, int H1, int W1, int H2, int W2, int C, int radius, 
 }
 
 // Library-owned scratch for the reference-compatible launchers, which take no
-// workspace argument. One buffer per device, grown with stream-ordered
-// cudaMallocAsync; the previous buffer is released with cudaFreeAsync on the
-// same stream, so no host synchronisation is needed.
+// workspace argument. One buffer per device, shared by every stream:
+//  * a call on stream s first makes s wait for the event recorded after the
+//    previous call's kernels (on whatever stream they ran), so two calls
+//    never use the buffer at the same time and a buffer is only freed after
+//    its last user has finished;
+//  * growing it frees the old buffer (cudaFreeAsync) and allocates the new
+//    one (cudaMallocAsync) on s, after that wait;
+//  * the lease holds the lock from the wait until the event is recorded
+//    behind the call's kernels, so host threads cannot interleave.
 struct DeviceScratch {
   void* ptr = nullptr;
   size_t bytes = 0;
+  cudaEvent_t done = nullptr;  // recorded after the last call that used ptr
+  cudaStream_t last = nullptr;
+  bool used = false;
 };
 std::mutex g_scratch_mu;
 DeviceScratch g_scratch[64];
 
-void* library_scratch(size_t bytes, cudaStream_t s) {
-  if (bytes == 0) return nullptr;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return nullptr;
-  std::lock_guard<std::mutex> lock(g_scratch_mu);
-  DeviceScratch& d = g_scratch[dev];
-  if (d.bytes >= bytes) return d.ptr;
-  if (d.ptr) cudaFreeAsync(d.ptr, s);
-  d.ptr = nullptr;
-  d.bytes = 0;
-  void* p = nullptr;
-  if (cudaMallocAsync(&p, bytes, s) != cudaSuccess) {
-    cudaGetLastError();
-    set_error("could not allocate " + std::to_string(bytes) + " B of scratch");
-    return nullptr;
+class ScratchLease {
+ public:
+  ScratchLease(size_t bytes, cudaStream_t s) : lock_(g_scratch_mu), s_(s) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+      cudaGetLastError();
+      set_error("no current CUDA device for the library scratch");
+      return;
+    }
+    d_ = &g_scratch[dev];
+    if (!d_->done && cudaEventCreateWithFlags(&d_->done, cudaEventDisableTiming) != cudaSuccess) {
+      cudaGetLastError();
+      d_->done = nullptr;
+      set_error("could not create the library scratch event");
+      d_ = nullptr;
+      return;
+    }
+    if (d_->used && d_->last != s &&
+        cudaStreamWaitEvent(s, d_->done, 0) != cudaSuccess) {
+      check_launch("wait for the previous user of the library scratch");
+      d_ = nullptr;
+      return;
+    }
+    if (bytes > d_->bytes) {
+      if (d_->ptr) cudaFreeAsync(d_->ptr, s);
+      d_->ptr = nullptr;
+      d_->bytes = 0;
+      void* p = nullptr;
+      if (cudaMallocAsync(&p, bytes, s) != cudaSuccess) {
+        cudaGetLastError();
+        set_error("could not allocate " + std::to_string(bytes) + " B of scratch");
+        d_ = nullptr;
+        return;
+      }
+      d_->ptr = p;
+      d_->bytes = bytes;
+    }
+    ptr_ = d_->ptr;
   }
-  d.ptr = p;
-  d.bytes = bytes;
-  return p;
-}
+  // Record the event behind everything this call enqueued on s.
+  ~ScratchLease() {
+    if (!d_) return;
+    if (cudaEventRecord(d_->done, s_) == cudaSuccess) {
+      d_->used = true;
+      d_->last = s_;
+    } else {
+      cudaGetLastError();
+    }
+  }
+  void* ptr() const { return ptr_; }
+  bool ok() const { return d_ != nullptr; }
+
+ private:
+  std::lock_guard<std::mutex> lock_;
+  cudaStream_t s_;
+  DeviceScratch* d_ = nullptr;
+  void* ptr_ = nullptr;
+};
 
 bool use_tc(int engine, int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
             int dilation,
@@ -213,10 +259,12 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
   if (use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &ok, false, f1, f2)) {
     const size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, false);
     if (lib_ws) {
-      ws = library_scratch(need, s);
-      ws_bytes = ws ? need : 0;
-      if (!ws && need) return false;
-    } else if (ws_bytes < need || (need && ws == nullptr)) {
+      ScratchLease lease(need, s);
+      if (!lease.ok()) return false;
+      return tc_forward(f1, f2, co, out, B, H1, W1, H2, W2, C, radius, levels, cdtype, ymajor,
+                        scale, lease.ptr(), need, s);
+    }
+    if (ws_bytes < need || (need && ws == nullptr)) {
       set_error("workspace too small: need " + std::to_string(need) + " B, got " +
                 std::to_string(ws_bytes));
       return false;
@@ -253,10 +301,12 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
   if (use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &ok, true, f1, f2)) {
     const size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, true);
     if (lib_ws) {
-      ws = library_scratch(need, s);
-      ws_bytes = ws ? need : 0;
-      if (!ws && need) return false;
-    } else if (ws_bytes < need || (need && ws == nullptr)) {
+      ScratchLease lease(need, s);
+      if (!lease.ok()) return false;
+      return tc_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels,
+                         cdtype, ymajor, scale, acc1, lease.ptr(), need, s);
+    }
+    if (ws_bytes < need || (need && ws == nullptr)) {
       set_error("workspace too small: need " + std::to_string(need) + " B, got " +
                 std::to_string(ws_bytes));
       return false;

@@ -747,8 +747,8 @@ __device__ __forceinline__ void gint_tile(const __half* __restrict__ tile, uint4
                                           int l, int b, const void* __restrict__ coords,
                                           int coords_f32, const int* __restrict__ inv,
                                           uint4* __restrict__ gsh, int* __restrict__ sbase,
-                                          __half* __restrict__ grad_f1, float scale, int ymajor,
-                                          int acc_f1, const TcGeom& g) {
+                                          __half* __restrict__ grad_f1, int ymajor, int acc_f1,
+                                          const TcGeom& g) {
   using S = GintShape<RADIUS>;
   constexpr int RD = S::RD, NG = S::NG, NU = S::NU, RC = S::RC, SU = S::SU;
   constexpr unsigned FULL = 0xffffffffu;
@@ -789,7 +789,9 @@ __device__ __forceinline__ void gint_tile(const __half* __restrict__ tile, uint4
   const int a = (x0 - RADIUS) & 7;
   const uint32_t sel = (a & 1) ? 0x5432u : 0x7654u;
   const bool s1 = (a & 2) != 0, s2 = (a & 4) != 0;
-  const float ex = 1.f - dx, ey = (1.f - dy) * scale, fy = dy * scale;
+  // The output scale is applied in float32 by the GEMM epilogues, not here:
+  // the float16 records keep the magnitude of the incoming gradient.
+  const float ex = 1.f - dx, ey = 1.f - dy, fy = dy;
   auto tap = [&](int iy, int ix) -> float {
     return __half2float(tile[(ymajor ? (ix + RD * iy) : (iy + RD * ix)) * 128 + t]);
   };
@@ -854,7 +856,7 @@ template <int RADIUS>
 __global__ void __launch_bounds__(128)
 tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
                int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
-               int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale, int ymajor,
+               int* __restrict__ sbase, __half* __restrict__ grad_f1, int ymajor,
                int vec_ok, int acc_f1, TcGeom g) {
   using S = GintShape<RADIUS>;
   constexpr int RD = S::RD, SU = S::SU;
@@ -881,7 +883,7 @@ tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ co
     }
   }
   __syncthreads();
-  gint_tile<RADIUS>(tile, stage, pix0, l, b, coords, coords_f32, inv, gsh, sbase, grad_f1, scale,
+  gint_tile<RADIUS>(tile, stage, pix0, l, b, coords, coords_f32, inv, gsh, sbase, grad_f1,
                     ymajor, acc_f1, g);
 }
 
@@ -893,7 +895,7 @@ template <int RADIUS>
 __global__ void __launch_bounds__(128)
 tc_gint_tma_kernel(const __grid_constant__ CUtensorMap tmap_g, const void* __restrict__ coords,
                    int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
-                   int* __restrict__ sbase, __half* __restrict__ grad_f1, float scale,
+                   int* __restrict__ sbase, __half* __restrict__ grad_f1,
                    int ymajor, int acc_f1, int nblk, int nruns, TcGeom g) {
   using S = GintShape<RADIUS>;
   constexpr int RD = S::RD;
@@ -937,8 +939,7 @@ tc_gint_tma_kernel(const __grid_constant__ CUtensorMap tmap_g, const void* __res
     const int pb = k - bl * nblk;
     const int b = bl / g.L, l = bl - b * g.L;
     gint_tile<RADIUS>(reinterpret_cast<const __half*>(gsm + buf * S::tile_pad), stage, pb * 128,
-                      l, b, coords, coords_f32, inv, gsh, sbase, grad_f1, scale, ymajor, acc_f1,
-                      g);
+                      l, b, coords, coords_f32, inv, gsh, sbase, grad_f1, ymajor, acc_f1, g);
     __syncthreads();
     pending_next = false;
   }
@@ -972,6 +973,7 @@ struct alignas(64) TcBwdParams {
   long long nitems;
   int nbg;     // grad_fmap1 builder groups (1 or 2)
   int acc_f1;  // add grad_fmap1 into the existing rows instead of overwriting them
+  float scale; // output scale, applied to the float32 accumulators
   TcGeom g;
 };
 
@@ -1221,10 +1223,8 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
         float v[32];
         tc::tmem_ld32(lane_addr + buf * 256 + c0, v);
         tc::tmem_ld_wait();
-        if (!live) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = 0.f;
-        }
+        for (int i = 0; i < 32; ++i) v[i] = live ? v[i] * p.scale : 0.f;
         if (valid) {
           uint4* dst = reinterpret_cast<uint4*>(p.grad_f1 + (long long)gid * g.C + c0);
 #pragma unroll
@@ -1564,6 +1564,8 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         tc::tmem_ld32(lane_addr + buf * 256 + c0, v);
         tc::tmem_ld_wait();
         if (inmap) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] *= p.scale;
 #pragma unroll
           for (int i = 0; i < 32; i += 4) {
             if (v[i] != 0.f || v[i + 1] != 0.f || v[i + 2] != 0.f || v[i + 3] != 0.f)
@@ -1926,16 +1928,16 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
     const int per_sm = std::max(1, (int)((size_t)max_dyn_smem() / (smem0 + 1024)));
     const int grid = std::min(nruns, num_sms() * per_sm);
     k0<<<grid, 128, smem0, s>>>(gmap, p1.coords, p1.coords_f32, inv, gsh,
-                                const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, p1.acc_f1,
-                                nblk, nruns, g);
+                                const_cast<int*>(p1.sbase), p1.grad_f1, ymajor, p1.acc_f1, nblk,
+                                nruns, g);
   } else {
     dim3 ug((g.HW + 127) / 128, g.L, g.B);
     auto k0 = tc_gint_kernel<RADIUS>;
     const size_t smem0 = GS::smem_bytes;
     if (!ensure_smem_attr((const void*)k0, smem0)) return false;
     k0<<<ug, 128, smem0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gsh,
-                              const_cast<int*>(p1.sbase), p1.grad_f1, scale, ymajor, vec_ok,
-                              p1.acc_f1, g);
+                              const_cast<int*>(p1.sbase), p1.grad_f1, ymajor, vec_ok, p1.acc_f1,
+                              g);
   }
   count_launch();
   if (!check_launch("tc_gint")) return false;
@@ -2038,6 +2040,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.grad_f1 = static_cast<__half*>(f1g);
   p1.grad_f2 = f2g;
   p1.acc_f1 = acc_f1 ? 1 : 0;
+  p1.scale = scale;
   p1.g = g;
   p1.nitems = (long long)B * g.items_before[levels];
   TcBwdParams p2 = p1;
@@ -2078,29 +2081,18 @@ static __device__ __align__(256) unsigned char g_noalloc_scratch[LCB200_NOALLOC_
 
 namespace lcb200 {
 namespace {
-std::mutex g_noalloc_mu;
-void* g_noalloc_ptr[64] = {};
-
 // Device address of g_noalloc_scratch on the current device (the host-side
-// name is only a stand-in). Looked up once per device.
+// name is only a stand-in). Looked up on every call, so a context that was
+// torn down and re-created (cudaDeviceReset) never sees a stale address.
 void* noalloc_scratch_ptr() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
-    set_error("no-alloc forward: no current CUDA device");
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    set_error(std::string("no-alloc forward: cudaGetSymbolAddress failed: ") +
+              cudaGetErrorString(e));
     return nullptr;
   }
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      set_error(std::string("no-alloc forward: cudaGetSymbolAddress failed: ") +
-                cudaGetErrorString(e));
-      return nullptr;
-    }
-    g_noalloc_ptr[dev] = p;
-  }
-  return g_noalloc_ptr[dev];
+  return p;
 }
 }  // namespace
 
@@ -2113,8 +2105,8 @@ extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
   using namespace lcb200;
   clear_error();
   if (B <= 0 || (long long)H1 * W1 <= 0) return true;
-  if (levels < 1 || levels > kMaxLevels) {
-    set_error("levels must be in [1, 8] (got " + std::to_string(levels) + ")");
+  if (levels < 1 || levels > kMaxTcLevels) {
+    set_error("no-alloc forward: levels must be in [1, 4] (got " + std::to_string(levels) + ")");
     return false;
   }
   for (int l = 0; l < levels; ++l) {

@@ -141,6 +141,99 @@ def pyramid_corr_points(fmap1: torch.Tensor, fmap2: torch.Tensor, coords: torch.
     return torch.stack(res, dim=1)
 
 
+def _tap_setup(co, bi, hi, wi, lvl, radius):
+    """Level-lvl window base and bilinear weights of the pixels (bi, hi, wi)."""
+    cx = co[bi, 0, hi, wi] / float(2 ** lvl)
+    cy = co[bi, 1, hi, wi] / float(2 ** lvl)
+    x0f, y0f = torch.floor(cx), torch.floor(cy)
+    dx, dy = cx - x0f, cy - y0f
+    wts = [(1 - dx) * (1 - dy), dx * (1 - dy), (1 - dx) * dy, dx * dy]
+    return x0f.long() - radius, y0f.long() - radius, wts
+
+
+_CORNERS = ((0, 0), (1, 0), (0, 1), (1, 1))
+
+
+def pyramid_corr_points_grad_fmap1(fmap1: torch.Tensor, fmap2: torch.Tensor,
+                                   coords: torch.Tensor, levels: int, radius: int,
+                                   points: torch.Tensor, grad_out: torch.Tensor,
+                                   ymajor: bool = False) -> torch.Tensor:
+    """Gradient of sum(grad_out * pyramid_corr) w.r.t. fmap1 at a pixel subset.
+
+    points: int64 [N, 3] rows (b, h, w); grad_out [B, L, RD^2, H, W]
+    (unscaled: multiply by the output scale outside). Returns [N, C] float64:
+      gf1[p, c] = sum_l sum_(iy,ix) g[p, l, d] * bilinear(f2_l, tap)[c]
+    with the per-corner masks, as the reference backward accumulates its
+    fmap1 row (cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:870-899).
+    Dilation 1 (the tensor-core engine's configuration)."""
+    go = grad_out.double()
+    co = coords.double()
+    rd = 2 * radius + 1
+    bi, hi, wi = points[:, 0], points[:, 1], points[:, 2]
+    n, c = len(points), fmap1.shape[1]
+    acc = torch.zeros(n, c, dtype=torch.float64)
+    for lvl, f2l in enumerate(build_pyramid(fmap2.double(), levels)):
+        hl, wl = f2l.shape[-2:]
+        xb, yb, wts = _tap_setup(co, bi, hi, wi, lvl, radius)
+        for iy in range(rd):
+            for ix in range(rd):
+                d = ix + rd * iy if ymajor else iy + rd * ix
+                g = go[bi, lvl, d, hi, wi]
+                for k, (ox, oy) in enumerate(_CORNERS):
+                    xx, yy = xb + ix + ox, yb + iy + oy
+                    valid = (xx >= 0) & (xx < wl) & (yy >= 0) & (yy < hl)
+                    v = f2l[bi, :, yy.clamp(0, hl - 1), xx.clamp(0, wl - 1)]
+                    acc += (g * wts[k] * valid.double()).unsqueeze(1) * v
+    return acc
+
+
+def pyramid_corr_points_grad_levels(fmap1: torch.Tensor, fmap2: torch.Tensor,
+                                    coords: torch.Tensor, levels: int, radius: int,
+                                    positions: torch.Tensor, grad_out: torch.Tensor,
+                                    ymajor: bool = False) -> torch.Tensor:
+    """Gradient of sum(grad_out * pyramid_corr) w.r.t. the pyramid levels at
+    a subset of level positions (the packed float32 gradient the C ABI
+    backward writes, before the pyramid build's own gradient).
+
+    positions: int64 [N, 4] rows (b, l, y, x) with (y, x) inside level l.
+    Returns [N, C] float64: the sum over every pixel p of image b and every
+    tap/corner of p's level-l window that lands on (y, x) of
+      g[p, l, d] * w_corner(p) * fmap1[p]
+    which is the reference backward's atomic scatter
+    (cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:901-913) gathered at one
+    target. Dilation 1."""
+    go = grad_out.double()
+    co = coords.double()
+    f1 = fmap1.double()
+    b_all, c, h, w = f1.shape
+    rd = 2 * radius + 1
+    out = torch.zeros(len(positions), c, dtype=torch.float64)
+    for i, (b, lvl, y, x) in enumerate(positions.tolist()):
+        cx = co[b, 0] / float(2 ** lvl)
+        cy = co[b, 1] / float(2 ** lvl)
+        x0f, y0f = torch.floor(cx), torch.floor(cy)
+        dx, dy = cx - x0f, cy - y0f
+        xb = x0f.long() - radius
+        yb = y0f.long() - radius
+        # pixels whose window (grid rows/cols base .. base + rd) holds (y, x)
+        near = (x >= xb) & (x <= xb + rd) & (y >= yb) & (y <= yb + rd)
+        hs, ws = torch.nonzero(near, as_tuple=True)
+        if len(hs) == 0:
+            continue
+        wts = [(1 - dx) * (1 - dy), dx * (1 - dy), (1 - dx) * dy, dx * dy]
+        coef = torch.zeros(len(hs), dtype=torch.float64)
+        for k, (ox, oy) in enumerate(_CORNERS):
+            ix = x - ox - xb[hs, ws]
+            iy = y - oy - yb[hs, ws]
+            ok = (ix >= 0) & (ix < rd) & (iy >= 0) & (iy < rd)
+            ixc, iyc = ix.clamp(0, rd - 1), iy.clamp(0, rd - 1)
+            d = ixc + rd * iyc if ymajor else iyc + rd * ixc
+            g = go[b, lvl][d, hs, ws]
+            coef += g * wts[k][hs, ws] * ok.double()
+        out[i] = (coef.unsqueeze(1) * f1[b, :, hs, ws].T).sum(dim=0)
+    return out
+
+
 def _pixel_to_grid(coords: torch.Tensor, size: int) -> torch.Tensor:
     """Pixel coordinate -> grid_sample coordinate with align_corners=False
     (onnx_generic.py:34-42)."""

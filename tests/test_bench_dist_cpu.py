@@ -61,3 +61,22 @@ def test_two_gloo_ranks_time_max_launch_sum_and_shards():
 def test_single_process_helpers_are_identity():
     assert bench.max_over_ranks(3.5, None, "cpu") == 3.5
     assert bench.sum_over_ranks(7, None, "cpu") == 7
+
+
+def test_split_workload_ranks_take_slices_of_one_global_batch():
+    # The default workload splits one global batch over the ranks (strong
+    # scaling): rank k's inputs are images [k*B/N, (k+1)*B/N) of the batch a
+    # single process would generate.
+    base = dict(bench.CONFIGS["raft_cpu_case"], B=4, split=True, backward=True)
+    whole = dict(base)
+    host1, dev1 = bench.make_inputs(whole, 0, "cpu")
+    world = 2
+    for rank in range(world):
+        cfg = dict(base, global_B=4, B=4 // world)
+        host, dev = bench.make_inputs(cfg, rank, "cpu")
+        lo, hi = rank * 2, rank * 2 + 2
+        assert torch.equal(host["f1"], host1["f1"][lo:hi])
+        assert torch.equal(host["f2"], host1["f2"][lo:hi])
+        assert all(torch.equal(a, b[lo:hi]) for a, b in zip(host["coords"], host1["coords"]))
+        assert all(torch.equal(a, b[lo:hi]) for a, b in zip(dev["grads"], dev1["grads"]))
+    assert bench.CONFIGS[bench.DEFAULT].get("split")

@@ -218,3 +218,35 @@ def test_tc_backward_config2_shape_adjoint():
     rhs2 = (g.double() * c2.double()).sum().item()
     assert abs(lhs1 - rhs1) <= 2e-3 * (abs(rhs1) + (g.double().norm() * c1.double().norm()).item() * 1e-2)
     assert abs(lhs2 - rhs2) <= 2e-3 * (abs(rhs2) + (g.double().norm() * c2.double().norm()).item() * 1e-2)
+
+
+def test_reference_abi_scratch_alternating_streams():
+    # The reference-compatible launcher takes no workspace; its library
+    # scratch is one buffer per device. Calls alternate between two streams
+    # with growing (then shrinking) shapes, so the buffer is regrown while
+    # the other stream's call may still run; each call still matches the
+    # oracle.
+    lib = _lib.load_library()
+    streams = [torch.cuda.Stream(), torch.cuda.Stream()]
+    shapes = [(1, 128, 24, 40), (2, 128, 48, 64), (2, 256, 64, 96), (1, 128, 30, 44),
+              (2, 256, 72, 100)]
+    runs = []
+    for i, (b, c, h, w) in enumerate(shapes):
+        f1, f2, co, fm1, packed = _inputs(b, c, h, w, 4, "gauss_oob", seed=70 + i)
+        co16 = co.half()
+        cod = co16.to(DEV)
+        out = torch.empty((b, 4, 81, h, w), dtype=torch.float16, device=DEV)
+        st = streams[i % 2]
+        st.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(st):
+            ok = lib.launchLocalCorrCudaPyramidForward(
+                fm1.data_ptr(), packed.data_ptr(), cod.data_ptr(), out.data_ptr(), b, h, w, c,
+                4, 4, 1, True, False, st.cuda_stream)
+        assert ok, _lib.last_error(lib)
+        runs.append((f1, f2, co16, fm1, packed, cod, out))
+    torch.cuda.synchronize()
+    for f1, f2, co16, _, _, _, out in runs:
+        c = f1.shape[1]
+        ref = oracle.pyramid_corr(f1.float(), f2.float(), co16.float(), 4, 4)
+        s = 1.0 / math.sqrt(c)
+        torch.testing.assert_close(out.double().cpu() * s, ref * s, **F16TOL)

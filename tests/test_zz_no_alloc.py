@@ -89,3 +89,39 @@ def test_no_alloc_rejects_oversize_and_unsupported(lib):
         f32.data_ptr(), f32.data_ptr(), f32.data_ptr(), out.data_ptr(), 1, 8, 8, 64, 4, 1,
         _lib.F32, _lib.F32, False, 1.0, torch.cuda.current_stream().cuda_stream)
     assert not ok and "tensor-core" in _lib.last_error(lib)
+
+
+def test_no_alloc_leaves_device_memory_untouched(lib):
+    # After a first call (which may load the library's device code), further
+    # calls take no device memory: the free byte count of the device stays
+    # the same across a call and its completion.
+    fm1, packed, coords = _case(11)
+    radius, levels = 4, 4
+    b, h, w, c = fm1.shape
+    out = torch.empty((b, levels, 81, h, w), dtype=torch.float16, device=DEV)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call():
+        return lib.launchLocalCorrB200PyramidForwardNoAlloc(
+            fm1.data_ptr(), packed.data_ptr(), coords.data_ptr(), out.data_ptr(), b, h, w, c,
+            radius, levels, _lib.F16, _lib.F16, False, 1.0 / 16, stream)
+
+    assert call(), _lib.last_error(lib)
+    torch.cuda.synchronize()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(3):
+        assert call(), _lib.last_error(lib)
+    torch.cuda.synchronize()
+    free_after, _ = torch.cuda.mem_get_info()
+    assert free_after == free_before
+
+
+def test_no_alloc_rejects_levels_beyond_four(lib):
+    fm1, packed, coords = _case(13, levels=4)
+    b, h, w, c = fm1.shape
+    out = torch.empty((b, 5, 81, h, w), dtype=torch.float16, device=DEV)
+    ok = lib.launchLocalCorrB200PyramidForwardNoAlloc(
+        fm1.data_ptr(), packed.data_ptr(), coords.data_ptr(), out.data_ptr(), b, h, w, c, 4, 5,
+        _lib.F16, _lib.F16, False, 1.0, torch.cuda.current_stream().cuda_stream)
+    assert not ok
+    assert "levels must be in [1, 4]" in _lib.last_error(lib)

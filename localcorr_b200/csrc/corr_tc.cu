@@ -30,10 +30,15 @@
 //             along W), zeros for dropped pixels.
 //
 // Warp roles of the forward kernel (persistent, one CTA per SM):
-//   warp 0      producer: cp.async gather of the A tile, TMA loads of B boxes
+//   warp 0      producer: TMA loads of the B boxes
 //   warp 1      TMEM owner and MMA issuer (one thread)
 //   warps 2..13 epilogue: three groups of four warps (TMEM lane quadrant =
-//               warp % 4) that share out the rows of each part
+//               warp % 4) that share out the rows of each part and stage
+//               each level's outputs in shared memory
+//   then        gather warps (cp.async of the A tile: the chunk's fmap1 rows)
+//               and copier warps (staged outputs -> the sorted scratch, one
+//               staging buffer behind the epilogue, so the epilogue never
+//               waits for the copy while the other buffer is free)
 // Every mbarrier wait is bounded (2 s); on timeout the kernel records an
 // error status, all roles wind down, TMEM is freed and the kernel returns.
 #include <cub/block/block_scan.cuh>
@@ -56,10 +61,14 @@ constexpr int kColBins = kCellX;  // sort bins per cell: the level-0 base column
 constexpr int kMaxTcLevels = 4;
 constexpr int kBwd1Threads = 64 + 256 + 128;  // grad_fmap1: producer, MMA, 2 x 4 builder warps, 4 epilogue warps
 constexpr int kFwdEG = 3;          // forward epilogue warp groups
-// forward fmap1 row gather (A tile): 4 warps, 2 at radius 8, whose
-// epilogue needs the registers of a smaller block
-constexpr int fwd_gather_warps(int radius) { return radius > 4 ? 2 : 4; }
-constexpr int fwd_threads(int radius) { return 64 + 128 * kFwdEG + 32 * fwd_gather_warps(radius); }
+// forward fmap1 row gather (A tile): 4 warps, 1 at radius 8, whose
+// epilogue needs the registers of a block of at most 512 threads
+constexpr int fwd_gather_warps(int radius) { return radius > 4 ? 1 : 4; }
+// staged-output copier warps
+constexpr int fwd_copy_warps(int radius) { return radius > 4 ? 1 : 2; }
+constexpr int fwd_threads(int radius) {
+  return 64 + 128 * kFwdEG + 32 * (fwd_gather_warps(radius) + fwd_copy_warps(radius));
+}
 
 // out[i] = v[rx + i] for rx in [0, 2^SD), a select network of SD stages on
 // the bits of rx (no dynamic register indexing).
@@ -216,6 +225,7 @@ struct alignas(64) TcFwdParams {
   int coords_f32;
   int ymajor;
   int nstage;
+  int nsb;  // output staging buffers (1 or 2)
   uint32_t stage_bytes;
   TcGeom g;
 };
@@ -441,19 +451,23 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = sA + g.KC * 16384;
+  constexpr int NCW = fwd_copy_warps(RADIUS);
   const int NST = p.nstage;
+  const int NSB = p.nsb;
   const int RDPS = g.RDP / 2 + 1;  // smem output row stride in 32-bit words (odd)
+  const int stage_words = kTile * RDPS;
   uint32_t* sOut = reinterpret_cast<uint32_t*>(sB + (size_t)NST * p.stage_bytes);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + kTile * RDPS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sOut + NSB * stage_words);
   uint64_t* full = bars;
   uint64_t* empty = bars + NST;
   uint64_t* a_full = bars + 2 * NST;
   uint64_t* a_empty = a_full + 1;
   uint64_t* t_full = a_full + 2;   // [2]
   uint64_t* t_empty = a_full + 4;  // [2]
-  uint64_t* epi_bar = a_full + 6;  // epilogue-wide sync (bounded, unlike bar.sync)
-  uint64_t* fin_bar = a_full + 7;  // all MMAs of this CTA complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_full + 8);
+  uint64_t* s_full = a_full + 6;   // [2] a level's outputs are staged
+  uint64_t* s_empty = a_full + 8;  // [2] a staging buffer has been copied out
+  uint64_t* fin_bar = a_full + 10; // all MMAs of this CTA complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(a_full + 11);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -465,7 +479,10 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
       tc::mbar_init(t_full + i, 1);
       tc::mbar_init(t_empty + i, kTile * kFwdEG);
     }
-    tc::mbar_init(epi_bar, kTile * kFwdEG);
+    for (int i = 0; i < 2; ++i) {
+      tc::mbar_init(s_full + i, kTile * kFwdEG);
+      tc::mbar_init(s_empty + i, 32 * NCW);
+    }
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
@@ -481,7 +498,48 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
   const int nwork = *p.work_count;
   volatile int* abort = &abort_flag;
 
-  if (warp >= 2 + 4 * kFwdEG) {
+  if (warp >= 2 + 4 * kFwdEG + GW) {
+    // ---------------- copier: staged level outputs -> sorted scratch ----------------
+    // Walks the same chunks and levels as the epilogue; staging buffer
+    // (chunk-level index) % NSB. The scratch rows are contiguous, so the
+    // copy is a flat run of 16-byte units (a row of RDP halves holds UPR of
+    // them); each thread loads four units' words from shared memory before
+    // storing them.
+    const int ct = threadIdx.x - (64 + 128 * kFwdEG + 32 * GW);
+    constexpr int NCT = 32 * NCW;
+    constexpr int RDP = ((2 * RADIUS + 1) * (2 * RADIUS + 1) + 7) / 8 * 8;
+    constexpr int UPR = RDP / 8;  // 16-byte units per scratch row
+    uint32_t li = 0;
+    bool ok = true;
+    for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x) {
+      const int4 wk = p.work[wi];
+      const int start = wk.z, n = wk.w;
+      for (int l = 0; l < g.L; ++l, ++li) {
+        const int sbuf = (int)(li % (uint32_t)NSB);
+        const uint32_t suse = li / (uint32_t)NSB;
+        if (!tc::mbar_wait(s_full + sbuf, suse & 1, abort)) { ok = false; break; }
+        const uint32_t* src = sOut + sbuf * stage_words;
+        uint4* dst = reinterpret_cast<uint4*>(p.scratch + ((long long)l * g.npix + start) * RDP);
+        const int nunits = n * UPR;
+        for (int u0 = ct; u0 < nunits; u0 += 4 * NCT) {
+          uint4 v[4];
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const int u = u0 + k * NCT;
+            if (u < nunits) {
+              const int row = u / UPR;
+              const uint32_t* sp = src + row * RDPS + (u - row * UPR) * 4;
+              v[k] = make_uint4(sp[0], sp[1], sp[2], sp[3]);
+            }
+          }
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            if (u0 + k * NCT < nunits) dst[u0 + k * NCT] = v[k];
+        }
+        tc::mbar_arrive(s_empty + sbuf);
+      }
+    }
+  } else if (warp >= 2 + 4 * kFwdEG) {
     // ---------------- A tile: the chunk's fmap1 rows ----------------
     // 128 rows x C fp16, K-major SWIZZLE_128B, 64-channel slabs. Warp gw
     // owns rows [gw * 128 / GW, (gw + 1) * 128 / GW); one copy instruction covers 4 rows x
@@ -606,20 +664,9 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
     const int q = warp & 3;               // TMEM lane quadrant of this warp
     const int ge = (warp - 2) >> 2;       // epilogue group
     const int t = q * 32 + lane;          // tile row = pixel slot
-    const int et = threadIdx.x - 64;      // 0..128*kFwdEG-1 for the copy
-    // copy-out walk: word i = et + k * (128 * kFwdEG) of the staged block as
-    // (row, word in row), advanced without a division per word
-    const int words = g.RDP / 2;
-    const int et_row = et / words, et_w = et - et_row * words;
-    const int step_rows = (kTile * kFwdEG) / words;
-    const int step_w = (kTile * kFwdEG) - step_rows * words;
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
-    uint32_t pc = 0, ephase = 0;
+    uint32_t pc = 0, li = 0;
     bool ok = true;
-    auto epi_sync = [&]() -> bool {
-      tc::mbar_arrive(epi_bar);
-      return tc::mbar_wait(epi_bar, (ephase++) & 1, abort);
-    };
     for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x) {
       const int4 wk = p.work[wi];
       const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
@@ -638,7 +685,11 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
       }
       const int ccy = cell / g.ncx, ccx = cell - ccy * g.ncx;
       const int cell_y0 = g.ylo + ccy * kCellY, cell_x0 = g.xlo + ccx * kCellX;
-      for (int l = 0; l < g.L && ok; ++l) {
+      for (int l = 0; l < g.L && ok; ++l, ++li) {
+        const int sbuf = (int)(li % (uint32_t)NSB);
+        const uint32_t suse = li / (uint32_t)NSB;
+        // the staging buffer's previous level has been copied out
+        if (!tc::mbar_wait(s_empty + sbuf, (suse & 1) ^ 1, abort)) { ok = false; break; }
         const float inv = 1.f / (float)(1 << l);
         const float clx = cx * inv, cly = cy * inv;
         const float x0f = floorf(clx), y0f = floorf(cly);
@@ -648,7 +699,7 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
         const int rx = (int)x0f - (cell_x0 >> l);   // 0..15
         const int ry = (int)y0f - (cell_y0 >> l);
         const int UW = g.UW[l], UH = g.UH[l], R = g.R[l];
-        __half* orow = reinterpret_cast<__half*>(sOut + t * RDPS);
+        __half* orow = reinterpret_cast<__half*>(sOut + sbuf * stage_words + t * RDPS);
         for (int k = 0; k < g.nparts[l]; ++k, ++pc) {
           const int buf = pc & 1;
           if (!tc::mbar_wait(t_full + buf, (pc >> 1) & 1, abort)) { ok = false; break; }
@@ -673,17 +724,8 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
           tc::mbar_arrive(t_empty + buf);
         }
         if (!ok) break;
-        // Level complete for this chunk: copy the staged rows to the scratch.
-        if (!epi_sync()) { ok = false; break; }
-        uint32_t* dst = reinterpret_cast<uint32_t*>(p.scratch + ((long long)l * g.npix + start) * g.RDP);
-        int row = et_row, wd2 = et_w;
-        for (int i = et; i < n * words; i += kTile * kFwdEG) {
-          dst[i] = sOut[row * RDPS + wd2];
-          row += step_rows;
-          wd2 += step_w;
-          if (wd2 >= words) { wd2 -= words; ++row; }
-        }
-        if (!epi_sync()) { ok = false; break; }
+        // Level complete for this chunk: hand the staged rows to the copier.
+        tc::mbar_arrive(s_full + sbuf);
       }
     }
   }
@@ -1022,8 +1064,9 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
   const int NST = p.nstage;
   const uint32_t SB = p.stage_bytes;  // 16 KB of A + KC * 8 KB of B
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * SB);
-  uint64_t* bfull = bars;
-  uint64_t* afull = bars + NST;
+  // full[s]: the stage's B boxes (TMA bytes, one producer arrival) and its A
+  // rows (one arrival per builder thread when its copies have landed)
+  uint64_t* full = bars;
   uint64_t* empty = bars + 2 * NST;
   uint64_t* acc_full = bars + 3 * NST;   // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
@@ -1039,8 +1082,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
   tc::fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
-      tc::mbar_init(bfull + s, 1);
-      tc::mbar_init(afull + s, kTile);
+      tc::mbar_init(full + s, kTile + 1);
       tc::mbar_init(empty + s, 1);
     }
     for (int i = 0; i < 2; ++i) { tc::mbar_init(acc_full + i, 1); tc::mbar_init(acc_empty + i, kTile); }
@@ -1079,10 +1121,10 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
             const uint32_t use = gs / NST;
             ++gs;
             if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
-            tc::mbar_arrive_expect_tx(bfull + s, box * g.KC);
+            tc::mbar_arrive_expect_tx(full + s, box * g.KC);
             uint8_t* sb = smem + (size_t)s * SB + 16384;
             for (int kc = 0; kc < g.KC; ++kc)
-              tc::tma_load_4d(sb + kc * 8192, &p.tmap[l], bfull + s, kc * 64, X0,
+              tc::tma_load_4d(sb + kc * 8192, &p.tmap[l], full + s, kc * 64, X0,
                               Y0 + gi * g.Rg[l], b);
           }
         }
@@ -1122,8 +1164,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
             if (++s == NST) { s = 0; ph ^= 1; }
             const uint64_t ad = a_desc0 + (uint64_t)(cs * stage_units);
             const uint64_t bd = b_desc0 + (uint64_t)(cs * stage_units);
-            if (!tc::mbar_wait(bfull + cs, cph, abort) ||
-                !tc::mbar_wait(afull + cs, cph, abort)) { ok = false; break; }
+            if (!tc::mbar_wait(full + cs, cph, abort)) { ok = false; break; }
             // A rows arrive through cp.async completion: make their
             // shared-memory writes visible to the tensor core's proxy.
             tc::fence_proxy_async_smem();
@@ -1190,7 +1231,7 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
             if (++uc == UPR) { uc = 0; ++br; }
           }
           tc::fence_proxy_async_smem();
-          tc::cp_async_mbar_arrive_noinc(afull + s);
+          tc::cp_async_mbar_arrive_noinc(full + s);
         }
       }
     }
@@ -1343,14 +1384,17 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   constexpr int NU = (NG + 14) / 8;
   extern __shared__ uint8_t smem_raw[];
   __shared__ int abort_flag;
-  __shared__ int stage_flags[8];   // 1: last stage of its item
+  // stages of each item, written by the TMA producer before the item's first
+  // stage is released (ring of 16 > the most items the producer can lead by)
+  __shared__ int item_nst[16];
   const TcGeom& g = p.g;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = p.nstage;
   const uint32_t SB = p.stage_bytes;  // A: 2 x 8 KB (position halves), B: KC x 8 KB
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + (size_t)NST * SB);
-  uint64_t* afull = bars;
-  uint64_t* bfull = bars + NST;
+  // full[s]: the stage's B tile (TMA bytes, one producer arrival) and its A
+  // rows (one arrival per builder thread when its copies have landed)
+  uint64_t* full = bars;
   uint64_t* empty = bars + 2 * NST;
   uint64_t* acc_full = bars + 3 * NST;   // [2]
   uint64_t* acc_empty = acc_full + 2;    // [2]
@@ -1364,15 +1408,13 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   tc::fence_proxy_async_smem();
   if (threadIdx.x == 0) {
     for (int s = 0; s < NST; ++s) {
-      tc::mbar_init(afull + s, kB2Rows);
-      tc::mbar_init(bfull + s, 1);
+      tc::mbar_init(full + s, kB2Rows + 1);
       tc::mbar_init(empty + s, 1);
     }
     for (int i = 0; i < 2; ++i) { tc::mbar_init(acc_full + i, 1); tc::mbar_init(acc_empty + i, kTile); }
     tc::mbar_init(fin_bar, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
-    for (int i = 0; i < 8; ++i) stage_flags[i] = 0;
   }
   if (warp == 0) {
     tc::tmem_alloc(tmem_slot, 512);
@@ -1404,26 +1446,21 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         const int buf = ac & 1;
         if (!tc::mbar_wait(acc_empty + buf, ((ac >> 1) & 1) ^ 1, abort)) break;
         tc::tc_fence_after();
-        bool first = true;
-        for (;;) {
+        int nst = 1;
+        for (int q = 0; q < nst; ++q) {
           const int cs = s;
           const uint32_t cph = ph;
           if (++s == NST) { s = 0; ph ^= 1; }
-          const uint64_t ad = a_desc0 + (uint64_t)(cs * stage_units);
-          const uint64_t bd = b_desc0 + (uint64_t)(cs * stage_units);
-          if (!tc::mbar_wait(bfull + cs, cph, abort) ||
-              !tc::mbar_wait(afull + cs, cph, abort)) { ok = false; break; }
+          if (!tc::mbar_wait(full + cs, cph, abort)) { ok = false; break; }
+          if (q == 0) nst = item_nst[ac & 15];
           // A rows arrive through cp.async completion: make their
           // shared-memory writes visible to the tensor core's proxy.
           tc::fence_proxy_async_smem();
           tc::tc_fence_after();
-          const int flags = stage_flags[cs];
-          stage_flags[cs] = 0;
           static_assert(kB2Rows / 16 == 4, "one 4-MMA batch per stage");
-          tc::mma_f16_ss_n(tmem + buf * 256, ad, 128, bd, 128, idesc, first ? 0u : 1u, 4);
-          first = false;
+          tc::mma_f16_ss_n(tmem + buf * 256, a_desc0 + (uint64_t)(cs * stage_units), 128,
+                           b_desc0 + (uint64_t)(cs * stage_units), 128, idesc, q ? 1u : 0u, 4);
           tc::mma_commit(empty + cs);
-          if (flags & 1) break;
         }
         if (!ok) break;
         tc::mma_commit(acc_full + buf);
@@ -1439,9 +1476,9 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     // a range's end belong to other cells (or are zero fill past the end);
     // their A rows are zero.
     if (lane == 0) {
-      uint32_t gs = 0;
+      uint32_t gs = 0, ic = 0;
       bool ok = true;
-      for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+      for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++ic) {
         const Bwd2Item item = decode_item(g, it, RADIUS);
         const int nr = item.empty ? 0 : item.rb - item.ra + 1;
         int2 rgs[kBwd2MaxRanges];
@@ -1462,10 +1499,12 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           const int s = gs % NST;
           const uint32_t use = gs / NST;
           if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
-          tc::mbar_arrive_expect_tx(bfull + s, bbytes);
+          // the item's stage count, released with its first stage
+          if (q == 0) item_nst[ic & 15] = last + 1;
+          tc::mbar_arrive_expect_tx(full + s, bbytes);
           uint8_t* sb = smem + (size_t)s * SB + 2 * kB2Rows * 128;
           for (int kc = 0; kc < g.KC; ++kc)
-            tc::tma_load_2d(sb + kc * kB2Rows * 128, &p.tmap_f1s, bfull + s, kc * 64, row);
+            tc::tma_load_2d(sb + kc * kB2Rows * 128, &p.tmap_f1s, full + s, kc * 64, row);
         }
       }
     }
@@ -1476,9 +1515,9 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     // stages with gs % 4 == gb: row t is candidate s0 + 64 j + t of the
     // stage's range, its G restricted to Q as 8 tile rows x two 16-byte
     // units, each a cp.async of a pre-shifted record unit or zeros (rows
-    // past the range and non-touching candidates come out all zero). The
-    // copies arrive on afull by themselves (cp.async.mbarrier.arrive.noinc);
-    // the builder of an item's last stage marks it for the MMA issuer.
+    // past the range and non-touching candidates come out all zero). Each
+    // builder's arrival on the stage's full barrier fires when its copies
+    // have landed (cp.async.mbarrier.arrive.noinc).
     const int bt = threadIdx.x - 64;
     const int gb = bt / kB2Rows;
     const int t = bt % kB2Rows;
@@ -1515,7 +1554,6 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
         const int s = gs % NST;
         const uint32_t use = gs / NST;
         if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
-        if (t == 0 && q == last) stage_flags[s] = 1;
         uint8_t* A = smem + (size_t)s * SB;
         const int sw = t & 7;  // 16-byte units XOR-swizzled by row (SW128)
         const int x0 = (int)(short)(pk & 0xFFFF), y0 = pk >> 16;
@@ -1537,8 +1575,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           }
         }
         tc::fence_proxy_async_smem();
-        __threadfence_block();  // the stage flag and zero stores before the arrival
-        tc::cp_async_mbar_arrive_noinc(afull + s);
+        tc::cp_async_mbar_arrive_noinc(full + s);
       }
     }
     // Copies still in flight complete before the kernel's final barrier.
@@ -1732,12 +1769,12 @@ bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStr
   return check_launch("tc_scatter");
 }
 
-size_t fwd_smem_bytes(const TcGeom& g, int nstage, uint32_t* stage_bytes) {
+size_t fwd_smem_bytes(const TcGeom& g, int nstage, int nsb, uint32_t* stage_bytes) {
   const uint32_t sb = (uint32_t)g.maxN * 128;
   if (stage_bytes) *stage_bytes = sb;
   const size_t rdps = g.RDP / 2 + 1;
   const size_t need = 1024 /*alignment slack*/ + (size_t)g.KC * 16384 + (size_t)nstage * sb +
-                      (size_t)kTile * rdps * 4 + (2 * nstage + 8) * 8 + 16;
+                      (size_t)nsb * kTile * rdps * 4 + (2 * nstage + 12) * 8 + 16;
   // At least half of the SM's shared memory: one CTA per SM, so the
   // 512-column TMEM allocation never waits on a co-resident CTA.
   return std::max<size_t>(need, 120 * 1024);
@@ -1745,9 +1782,25 @@ size_t fwd_smem_bytes(const TcGeom& g, int nstage, uint32_t* stage_bytes) {
 
 bool radius_supported(int r) { return r == 3 || r == 4 || r == 8; }
 
+// Forward pipeline depth: two output staging buffers when that still leaves
+// three B stages, else one; then as many B stages (<= 4) as fit.
+bool fwd_pipeline(const TcGeom& g, int* nstage, int* nsb) {
+  const size_t lim = (size_t)max_dyn_smem();
+  for (int sb = 2; sb >= 1; --sb) {
+    int nst = 4;
+    while (nst >= 2 && fwd_smem_bytes(g, nst, sb, nullptr) > lim) --nst;
+    if (nst >= (sb == 2 ? 3 : 2)) {
+      *nstage = nst;
+      *nsb = sb;
+      return true;
+    }
+  }
+  return false;
+}
+
 bool eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
               int dilation, int dtype, std::string* why, TcGeom* out_geom,
-              int* out_nstage) {
+              int* out_nstage, int* out_nsb = nullptr) {
   auto no = [&](const char* m) { if (why) *why = m; return false; };
   if (dtype != LCB200_F16) return no("tensor-core engine needs float16 maps");
   if (dilation != 1) return no("tensor-core engine needs dilation 1");
@@ -1757,12 +1810,11 @@ bool eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int leve
   TcGeom g;
   if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, why)) return false;
   if ((long long)B * H1 * W1 >= (1ll << 31)) return no("too many pixels");
-  const size_t lim = (size_t)max_dyn_smem();
-  int nst = 4;
-  while (nst >= 2 && fwd_smem_bytes(g, nst, nullptr) > lim) --nst;
-  if (nst < 2) return no("tensor-core engine shared-memory budget exceeded");
+  int nst = 0, nsb = 0;
+  if (!fwd_pipeline(g, &nst, &nsb)) return no("tensor-core engine shared-memory budget exceeded");
   if (out_geom) *out_geom = g;
   if (out_nstage) *out_nstage = nst;
+  if (out_nsb) *out_nsb = nsb;
   return true;
 }
 
@@ -1794,9 +1846,9 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
                 int H2, int W2, int C, int radius, int levels, int cdtype, bool ymajor, float scale, void* ws,
                 size_t ws_bytes, cudaStream_t s) {
   TcGeom g;
-  int nst = 0;
+  int nst = 0, nsb = 0;
   std::string why;
-  if (!eligible(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &why, &g, &nst)) {
+  if (!eligible(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &why, &g, &nst, &nsb)) {
     set_error("tensor-core forward: " + why);
     return false;
   }
@@ -1847,8 +1899,9 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
   prm.coords_f32 = cdtype == LCB200_F32;
   prm.ymajor = ymajor ? 1 : 0;
   prm.nstage = nst;
+  prm.nsb = nsb;
   prm.g = g;
-  const size_t smem = fwd_smem_bytes(g, nst, &prm.stage_bytes);
+  const size_t smem = fwd_smem_bytes(g, nst, nsb, &prm.stage_bytes);
   bool ok = false;
   switch (radius) {
     case 3: ok = launch_fwd_kernel<3>(prm, smem, s); break;

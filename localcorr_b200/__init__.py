@@ -7,6 +7,7 @@ The kernels live in liblocalcorr_b200.so (C ABI: include/localcorr_b200.h),
 built with ``python -m localcorr_b200.csrc.build``.
 """
 
+from . import torch_ops  # noqa: F401  (registers torch.ops.localcorr.*)
 from .backend import get_onnx_backend, set_onnx_backend
 from .blocks import (
     LocalCorrCudaPyramidBlock,

@@ -228,8 +228,8 @@ class LocalCorrRowBandBlock:
         self.rows = (y0, y1)
         self.scale = 1.0 / math.sqrt(c)
         if hb > 0:
-            self.fmap1 = ops.NchwToNhwc.apply(fmap1_band)
-            local = ops.PyramidBuild.apply(fmap2_band, self.num_levels)
+            self.fmap1 = torch.ops.localcorr.nchw_to_nhwc(fmap1_band)
+            local = torch.ops.localcorr.pyramid_build(fmap2_band, self.num_levels)
         else:
             self.fmap1 = fmap1_band.new_empty((b, 0, w, c))
             local = fmap2_band.new_empty((b, 0))
@@ -251,7 +251,7 @@ class LocalCorrRowBandBlock:
         if hb == 0:
             return coords_band.new_empty((b, self.num_levels * rd * rd, 0, w),
                                          dtype=self.fmap1.dtype)
-        corr = ops.ScaledPyramidCorr.apply(self.fmap1, self.fmap2_packed, coords_band,
-                                           self.radius, self.num_levels, 1, False, self.scale,
-                                           (self.height, self.width))
+        corr = torch.ops.localcorr.pyramid_corr(self.fmap1, self.fmap2_packed, coords_band,
+                                                self.radius, self.num_levels, 1, False,
+                                                self.scale, self.height, self.width)
         return corr.reshape(b, -1, hb, w)

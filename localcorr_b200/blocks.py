@@ -230,15 +230,19 @@ class LocalCorrCudaPyramidBlock:
             raise RuntimeError(
                 "localcorr_b200 requires float32 or float16 feature maps of one dtype, but got "
                 f"{fmap1.dtype} and {fmap2.dtype}.")
-        self.fmap1 = ops.NchwToNhwc.apply(fmap1)
-        self.fmap2_packed = ops.PyramidBuild.apply(fmap2, self.num_levels)
+        self.fmap1 = torch.ops.localcorr.nchw_to_nhwc(fmap1)
+        self.fmap2_packed = torch.ops.localcorr.pyramid_build(fmap2, self.num_levels)
         # Lookups read detached copies of the prepared maps and send their
         # gradients through one token into shared accumulators (see
         # ops.LookupGrads); the attributes above stay differentiable for
         # callers that use them directly.
         self._grads = None
         self._token = None
-        if torch.is_grad_enabled() and (fmap1.requires_grad or fmap2.requires_grad):
+        # Under torch.compile the lookups stay registered custom operators
+        # (torch.ops.localcorr.pyramid_corr, one graph node each, no break);
+        # eagerly they share one pair of gradient accumulators.
+        if (torch.is_grad_enabled() and (fmap1.requires_grad or fmap2.requires_grad)
+                and not torch.compiler.is_compiling()):
             self._grads = ops.LookupGrads(self.fmap1.detach(), self.fmap2_packed.detach(),
                                           fmap2.shape, self.num_levels)
             self._token = ops.LookupGradSink.apply(fmap1, fmap2, self._grads)
@@ -269,8 +273,9 @@ class LocalCorrCudaPyramidBlock:
             corr = ops.PyramidLookup.apply(self._token, coords, self._grads, self.radius,
                                            self.num_levels, scale)
         else:
-            corr = ops.ScaledPyramidCorr.apply(self.fmap1, self.fmap2_packed, coords,
-                                               self.radius, self.num_levels, 1, False, scale)
+            corr = torch.ops.localcorr.pyramid_corr(self.fmap1, self.fmap2_packed, coords,
+                                                    self.radius, self.num_levels, 1, False,
+                                                    scale, 0, 0)
         return corr.reshape(b, -1, h, w)
 
     def _export(self, coords):

@@ -461,13 +461,14 @@ def spatial_corr(in1, in2, radius, dilation=1, scale=1.0) -> torch.Tensor:
     _dtype_code(in1)
     if in2.dtype != in1.dtype:
         raise RuntimeError("input1 and input2 must have the same dtype")
+    lc = torch.ops.localcorr
     if radius <= SPATIAL_KERNEL_MAX_RADIUS:
-        return SpatialCorr.apply(in1, in2, radius, dilation, scale)
+        return lc.spatial_corr(in1, in2, int(radius), int(dilation), float(scale))
     b, c, h, w = in1.shape
-    f1 = NchwToNhwc.apply(in1)
-    f2 = NchwToNhwc.apply(in2).reshape(b, -1)
+    f1 = lc.nchw_to_nhwc(in1)
+    f2 = lc.nchw_to_nhwc(in2).reshape(b, -1)
     coords = identity_coords(b, h, w, torch.float32, in1.device)
-    corr = ScaledPyramidCorr.apply(f1, f2, coords, radius, 1, dilation, True, scale)
+    corr = lc.pyramid_corr(f1, f2, coords, int(radius), 1, int(dilation), True, float(scale), 0, 0)
     rd = 2 * radius + 1
     return corr.view(b, rd, rd, h, w)
 

@@ -73,6 +73,15 @@ CONFIGS = {
                          coords="uniform64", fdist="uniform", backward=True),
     "highbatch_r8": dict(B=8, C=128, H=64, W=128, L=4, r=8, iters=1, dtype="f16",
                          coords="uniform64", fdist="uniform", backward=True),
+    # PWC-Net spatial correlation over a 5-level feature pyramid (benchmark
+    # configuration 3): B=8, patch 9, [C, H, W] per level
+    # (its 15 kernels are short, so the step is replayed from a CUDA graph)
+    "pwc_spatial_f32": dict(kind="spatial", B=8, r=4, iters=1, dtype="f32", backward=True,
+                            levels=[(196, 7, 16), (128, 14, 32), (96, 28, 64), (64, 56, 128),
+                                    (32, 112, 256)], split=True, graph=True),
+    "pwc_spatial_f16": dict(kind="spatial", B=8, r=4, iters=1, dtype="f16", backward=True,
+                            levels=[(196, 7, 16), (128, 14, 32), (96, 28, 64), (64, 56, 128),
+                                    (32, 112, 256)], split=True, graph=True),
 }
 DEFAULT = "raft_train_1080p"
 METRIC = "corr Glookups/s fwd+bwd (B*H*W*L*(2r+1)^2)"
@@ -115,6 +124,9 @@ def sum_over_ranks(value, dist, device):
 
 
 def lookups_per_call(cfg):
+    if cfg.get("kind") == "spatial":
+        # one call = every level of the pyramid: B*H*W*(2r+1)^2 per level
+        return sum(cfg["B"] * h * w for _, h, w in cfg["levels"]) * (2 * cfg["r"] + 1) ** 2
     return cfg["B"] * cfg["H"] * cfg["W"] * cfg["L"] * (2 * cfg["r"] + 1) ** 2
 
 
@@ -204,6 +216,48 @@ class ClockSampler:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def make_spatial_inputs(cfg, rank, device):
+    """Configuration 3 inputs: per level input1 ~ N(0,1), input2 = input1
+    rolled by an integer translation in [-4, 4]^2 per image plus N(0, 0.1^2)
+    noise, upstream gradients ~ N(0,1); the rank's slice of the global batch."""
+    g = torch.Generator().manual_seed(4321)
+    dt = torch.float16 if cfg["dtype"] == "f16" else torch.float32
+    gb = cfg.get("global_B", cfg["B"])
+    lo, hi = rank * cfg["B"], (rank + 1) * cfg["B"]
+    rd = 2 * cfg["r"] + 1
+    host = {"in1": [], "in2": []}
+    grads = []
+    for c, h, w in cfg["levels"]:
+        x1 = torch.randn(gb, c, h, w, generator=g)
+        x2 = torch.empty_like(x1)
+        for i in range(gb):
+            ty, tx = (int(v) for v in torch.randint(-4, 5, (2,), generator=g))
+            x2[i] = torch.roll(x1[i], shifts=(ty, tx), dims=(1, 2))
+        x2 += 0.1 * torch.randn(x2.shape, generator=g)
+        go = torch.randn(gb, rd, rd, h, w, generator=g)
+        pin = (lambda t: t.pin_memory()) if torch.cuda.is_available() else (lambda t: t)
+        host["in1"].append(pin(x1[lo:hi].to(dt).contiguous()))
+        host["in2"].append(pin(x2[lo:hi].to(dt).contiguous()))
+        grads.append(go[lo:hi].to(dt).contiguous())
+    dev = {"in1": [t.to(device) for t in host["in1"]],
+           "in2": [t.to(device) for t in host["in2"]],
+           "grads": [t.to(device) for t in grads]}
+    return host, dev
+
+
+def run_spatial_step(cfg, in1, in2, grads):
+    """One PWC step: the sampler (patch 9) forward on every level, then the
+    backward of all of them; returns the input gradients of every level."""
+    import localcorr_b200 as lc
+
+    sampler = lc.get_localcorr_sampler(patch_size=2 * cfg["r"] + 1, corr_mode="localcorr_cuda")
+    xs1 = [x.detach().requires_grad_(True) for x in in1]
+    xs2 = [x.detach().requires_grad_(True) for x in in2]
+    outs = [sampler(a, b) for a, b in zip(xs1, xs2)]
+    torch.autograd.backward(outs, grads)
+    return [x.grad for x in xs1], [x.grad for x in xs2]
 
 
 def make_inputs(cfg, rank, device):
@@ -303,12 +357,40 @@ def timed_loop(fn, steps, device):
     return start.elapsed_time(end) / 1e3
 
 
+def cpu_spatial_sample(cfg):
+    """Time the reference's standard-ops spatial correlation (shifted slices
+    of a zero-padded map, onnx_generic.py:159-198, restated as
+    oracle.spatial_corr) on the host cores: one image of every level,
+    float32, forward and backward."""
+    from oracle import oracle
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    r = cfg["r"]
+    g = torch.Generator().manual_seed(8)
+    t0 = time.perf_counter()
+    n = 0
+    for c, h, w in cfg["levels"]:
+        x1 = torch.randn(1, c, h, w, generator=g).requires_grad_(True)
+        x2 = torch.randn(1, c, h, w, generator=g).requires_grad_(True)
+        out = oracle.spatial_corr(x1, x2, r, dtype=torch.float32)
+        out.backward(torch.ones_like(out))
+        n += h * w * (2 * r + 1) ** 2
+    dt = time.perf_counter() - t0
+    return {"value": n / dt / 1e9, "unit": "Glookups/s", "cores": threads, "kind": "port",
+            "sample": "1 image of each of the 5 levels, fp32, fwd+bwd, "
+                      "oracle/oracle.py:spatial_corr (onnx_generic.py:159-198 form)",
+            "seconds": dt}
+
+
 def cpu_baseline_sample(cfg, seconds_hint=20.0):
     """Time the reference CPU formulation (restated in oracle/oracle.py) on a
     bounded sample: one image, a band of fmap1 rows, float32; forward and
     backward, or forward only for the forward-only workloads."""
     from oracle import oracle
 
+    if cfg.get("kind") == "spatial":
+        return cpu_spatial_sample(cfg)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     c, h, w, L, r = cfg["C"], cfg["H"], cfg["W"], cfg["L"], cfg["r"]
@@ -350,7 +432,8 @@ def reference_arm(args, cfg, cfg_name):
         "impl": "reference", "metric": metric_name(cfg), "value": v, "unit": "Glookups/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * t_total / max(1, args.steps), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "scaling": "strong" if (cfg.get("split") or cfg.get("bands")) else "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": cfg_name, "per_step": s["sample"]},
         "cpu_baseline": {k: s[k] for k in ("unit", "cores", "kind", "sample")} | {"value": v},
         "e2e": {"value": v, "unit": "Glookups/s", "h2d_bytes_per_step": 0,
@@ -403,10 +486,22 @@ def main(argv=None):
     from localcorr_b200 import _lib, ops
 
     lib = _lib.require_library()
-    host, dev = make_inputs(cfg, rank, device)
+    spatial = cfg.get("kind") == "spatial"
+    if spatial:
+        host, dev = make_spatial_inputs(cfg, rank, device)
+        names = ["in1", "in2"]
+
+        def step_on(x):
+            return run_spatial_step(cfg, x["in1"], x["in2"], dev["grads"])
+    else:
+        host, dev = make_inputs(cfg, rank, device)
+        names = ["f1", "f2", "coords"]
+
+        def step_on(x):
+            return run_step(cfg, x["f1"], x["f2"], x["coords"], dev["grads"])
 
     def step():
-        return run_step(cfg, dev["f1"], dev["f2"], dev["coords"], dev["grads"])
+        return step_on(dev)
 
     for _ in range(max(3, args.warmup)):
         step()
@@ -416,26 +511,64 @@ def main(argv=None):
         if dist is not None:
             dist.barrier()
 
+    use_graph = bool(cfg.get("graph"))
+
+    def capture(fn):
+        """Record one step of fn in a CUDA graph (after two warm-up runs on a
+        side stream, as torch.cuda.graph requires); returns the graph, the
+        step's (static) outputs and the library launches it holds."""
+        side = torch.cuda.Stream(device)
+        side.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fn()
+        torch.cuda.current_stream(device).wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        lib.localCorrB200LaunchCount(1)
+        with torch.cuda.graph(graph):
+            res = fn()
+        n = int(lib.localCorrB200LaunchCount(1))
+        torch.cuda.synchronize(device)
+        return graph, res, n
+
+    records = []
+    if use_graph:
+        # Per-kernel times come from an eager pass (events recorded inside a
+        # graph are not per replay); the timed steps replay the graph.
+        ops.set_launch_timer(records)
+        for _ in range(min(args.steps, 10)):
+            step()
+        torch.cuda.synchronize(device)
+        ops.set_launch_timer(None)
+        g_main, _, graph_launches = capture(step)
+        timed_step = g_main.replay
+    else:
+        timed_step = step
+
     # ---- timed region: device-resident inputs ----
     sampler = ClockSampler(local_rank) if rank == 0 else None
     if sampler:
         sampler.start()
-    records = []
-    ops.set_launch_timer(records)
+    if not use_graph:
+        ops.set_launch_timer(records)
     lib.localCorrB200LaunchCount(1)
     barrier()
-    elapsed = timed_loop(step, args.steps, device)
+    elapsed = timed_loop(timed_step, args.steps, device)
     barrier()
     launches = int(lib.localCorrB200LaunchCount(1))
+    if use_graph:
+        launches = graph_launches * args.steps  # replayed, not issued from the host
     ops.set_launch_timer(None)
     clocks = sampler.stop() if sampler else None
     elapsed = max_over_ranks(elapsed, dist, device)
     launches = int(sum_over_ranks(launches, dist, device))
 
-    # per-kernel durations from the live events
-    per = {}
-    for name, s, e in records:
-        per.setdefault(name, []).append(s.elapsed_time(e) / 1e3)
+    # per-kernel durations (and algorithmic bytes, where the op knows them)
+    # from the live events
+    per, per_bytes = {}, {}
+    for name, s_ev, e_ev, nb in records:
+        per.setdefault(name, []).append(s_ev.elapsed_time(e_ev) / 1e3)
+        per_bytes.setdefault(name, []).append(nb)
     kern = max(per, key=lambda k: sum(per[k])) if per else None
 
     # ---- end-to-end through the public API with host buffers ----
@@ -444,10 +577,33 @@ def main(argv=None):
     # step i+1 runs on a copy stream while step i computes (two device input
     # sets), as a training loop with a prefetching loader does; each step's
     # copy and read-back are inside the timed region.
-    dsets = [dict(f1=torch.empty_like(dev["f1"]), f2=torch.empty_like(dev["f2"]),
-                  coords=[torch.empty_like(c) for c in dev["coords"]]) for _ in range(2)]
+    def as_list(v):
+        return v if isinstance(v, list) else [v]
+
+    def shaped(flat):
+        """The step's input dict from a flat tensor list (order of names)."""
+        out, k = {}, 0
+        for n in names:
+            cnt = len(as_list(dev[n]))
+            out[n] = flat[k:k + cnt] if isinstance(dev[n], list) else flat[k]
+            k += cnt
+        return out
+
+    host_flat = [t for n in names for t in as_list(host[n])]
+    dsets = [[torch.empty_like(t) for n in names for t in as_list(dev[n])] for _ in range(2)]
+    if use_graph:
+        # one graph per device input set, so the copies of step i+1 still
+        # overlap step i
+        graphed = [capture(lambda d=d: step_on(shaped(d)))[:2] for d in dsets]
     copy_stream = torch.cuda.Stream(device)
     main_stream = torch.cuda.current_stream(device)
+
+    def checksum(g):
+        if g is None:
+            return 0.0
+        if isinstance(g, list):
+            return torch.stack([x.double().sum() for x in g]).sum()
+        return g.double().sum()
 
     def e2e_timed(steps):
         ready = [torch.cuda.Event() for _ in range(2)]
@@ -461,10 +617,8 @@ def main(argv=None):
             with torch.cuda.stream(copy_stream):
                 if i >= 2:
                     copy_stream.wait_event(freed[i % 2])
-                d["f1"].copy_(host["f1"], non_blocking=True)
-                d["f2"].copy_(host["f2"], non_blocking=True)
-                for dc, hc in zip(d["coords"], host["coords"]):
-                    dc.copy_(hc, non_blocking=True)
+                for dt_, ht_ in zip(d, host_flat):
+                    dt_.copy_(ht_, non_blocking=True)
                 ready[i % 2].record(copy_stream)
 
         torch.cuda.synchronize(device)
@@ -478,8 +632,12 @@ def main(argv=None):
                 issue_copy(i + 1)
             d = dsets[i % 2]
             main_stream.wait_event(ready[i % 2])
-            g1, g2 = run_step(cfg, d["f1"], d["f2"], d["coords"], dev["grads"])
-            chk = g1.double().sum() + (g2.double().sum() if g2 is not None else 0.0)
+            if use_graph:
+                graphed[i % 2][0].replay()
+                g1, g2 = graphed[i % 2][1]
+            else:
+                g1, g2 = step_on(shaped(d))
+            chk = checksum(g1) + checksum(g2)
             res_host[i:i + 1].copy_(chk.reshape(1), non_blocking=True)
             fetched[i].record(main_stream)
             freed[i % 2].record(main_stream)
@@ -501,8 +659,7 @@ def main(argv=None):
     shards = 1 if cfg.get("bands") else world  # row bands split one frame
     value = lookups_step * args.steps * shards / elapsed / 1e9
     e2e_value = lookups_step * args.steps * shards / e2e_elapsed / 1e9
-    h2d = (host["f1"].numel() + host["f2"].numel()) * host["f1"].element_size() + sum(
-        co.numel() * co.element_size() for co in host["coords"])
+    h2d = sum(t.numel() * t.element_size() for t in host_flat)
 
     line = None
     if rank == 0:
@@ -510,8 +667,14 @@ def main(argv=None):
         roof = None
         if kern:
             dur = statistics.mean(per[kern])
-            abytes = algorithmic_bytes(cfg, kern)
-            achieved = abytes / dur / 1e9
+            nbs = per_bytes[kern]
+            if all(nb is not None for nb in nbs):
+                # calls of different sizes (the levels of a pyramid)
+                abytes = sum(nbs) / len(nbs)
+                achieved = sum(nbs) / sum(per[kern]) / 1e9
+            else:
+                abytes = algorithmic_bytes(cfg, kern)
+                achieved = abytes / dur / 1e9
             traffic = None
             tf = ROOT / "profiles" / "traffic.json"
             if tf.exists():
@@ -534,16 +697,20 @@ def main(argv=None):
             "vs_baseline": None,
             "dtype": cfg["dtype"], "data": "synthetic",
             "config": {"workload": args.config, "B_per_gpu": cfg["B"], "global_batch":
-                       cfg["B"] * shards, "C": cfg["C"], "H": cfg["H"], "W": cfg["W"],
-                       "levels": cfg["L"], "radius": cfg["r"], "lookups_per_step":
-                       cfg["iters"], "backward": cfg["backward"],
+                       cfg["B"] * shards, "C": cfg.get("C"), "H": cfg.get("H"),
+                       "W": cfg.get("W"),
+                       "levels": cfg["levels"] if spatial else cfg["L"], "radius": cfg["r"],
+                       "lookups_per_step": cfg["iters"], "backward": cfg["backward"],
                        "parallelism": (f"row-band x{world}: one all-gather of the band "
                                        "pyramids per frame" if cfg.get("bands") else
                                        f"batch-split x{world}: {cfg['B']} of the global "
                                        f"{cfg['B'] * shards} images per rank, no collective"
                                        if cfg.get("split") else
                                        f"batch-shard x{world}, no collective"),
-                       "l2": "inputs larger than L2 (no flush)"},
+                       "l2": ("inputs larger than L2 (no flush)" if not spatial else
+                              "the step touches ~400/200 MB (fp32/fp16: inputs, "
+                              "correlations, their gradients), more than L2; no flush"),
+                       "cuda_graph": use_graph},
             "e2e": {"value": e2e_value, "unit": "Glookups/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": 8,
                     "note": "inputs of step i+1 copied on a second stream during step i; "

@@ -225,8 +225,9 @@ LCB200_API int localCorrB200DeviceStatus(int reset);
 /* Library ABI version (major*10000 + minor*100 + patch). */
 LCB200_API int localCorrB200Version(void);
 
-/* Number of kernel launches issued by this library on this thread since the
- * last reset (diagnostics for launch accounting in benchmarks). */
+/* Number of kernel launches issued by this library in this process (all
+ * host threads) since the last reset (diagnostics for launch accounting in
+ * benchmarks). */
 LCB200_API long long localCorrB200LaunchCount(int reset);
 
 #ifdef __cplusplus

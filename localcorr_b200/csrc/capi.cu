@@ -43,12 +43,14 @@ bool spatial_backward(const void*, const void*, const void*, void*, void*, int, 
 
 namespace {
 thread_local std::string g_last_error;
-thread_local long long g_launches = 0;
+// every host thread's launches (autograd runs backward passes on its own
+// worker threads)
+std::atomic<long long> g_launches{0};
 }  // namespace
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 void clear_error() { g_last_error.clear(); }
-void count_launch(int n) { g_launches += n; }
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 
 bool check_launch(const char* what) {
   const cudaError_t e = cudaGetLastError();
@@ -500,9 +502,7 @@ int localCorrB200DeviceStatus(int reset) { return tc_device_status(reset != 0); 
 int localCorrB200Version(void) { return 100; }
 
 long long localCorrB200LaunchCount(int reset) {
-  const long long v = g_launches;
-  if (reset) g_launches = 0;
-  return v;
+  return reset ? g_launches.exchange(0) : g_launches.load();
 }
 
 }  // extern "C"

@@ -10,6 +10,8 @@
 // several FMAs. The backward is two gathers (no atomics):
 //   grad_in1[c,p] = scale * sum_d g[d,p]     * in2[c,p+delta_d]
 //   grad_in2[c,q] = scale * sum_d g[d,q-delta_d] * in1[c,q-delta_d]
+#include <initializer_list>
+
 #include "lc_common.cuh"
 
 namespace lcb200 {
@@ -178,7 +180,7 @@ spatial_bwd_kernel(const T* __restrict__ gout, const T* __restrict__ X, T* __res
         const int col = SHIFTED ? px0 + i + 2 * R - dil * ix : px0 + i;
         gv[ix][i] = Gs[(ix * kTH + py) * SG + col];
       }
-#pragma unroll 2
+#pragma unroll
     for (int cc = 0; cc < CKt; ++cc) {
       const float* xr = Xs + ((cg * CKt + cc) * kTH + py) * SX + px0;
       if constexpr (DIL1) {
@@ -218,9 +220,312 @@ spatial_bwd_kernel(const T* __restrict__ gout, const T* __restrict__ X, T* __res
   }
 }
 
+// ---- tiled path: dilation 1, W % 4 == 0, aligned bases -------------------
+// Inputs stream into shared memory as units of 4 elements (16 B in float32,
+// 8 B in float16) with cp.async, zero-filled outside the image; a unit is
+// wholly inside or outside because W % 4 == 0 and units start on multiples
+// of 4. The next slab is copied while the current one is used (double
+// buffer). Shared rows are padded to a multiple of 4 elements plus 4, so the
+// 4-element reads of a warp's 8 pixel quads hit distinct banks.
+template <typename T>
+__device__ __forceinline__ void cp4(T* dst, const T* src, bool valid) {
+  if constexpr (sizeof(T) == 4) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid ? 16u : 0u)
+                 : "memory");
+  } else {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8, %2;" ::"r"(
+                     static_cast<uint32_t>(__cvta_generic_to_shared(dst))),
+                 "l"(src), "r"(valid ? 8u : 0u)
+                 : "memory");
+  }
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Four consecutive shared elements (4-element aligned) as floats.
+__device__ __forceinline__ void ld4(const float* p, float* o) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  o[0] = v.x; o[1] = v.y; o[2] = v.z; o[3] = v.w;
+}
+__device__ __forceinline__ void ld4(const __half* p, float* o) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  o[0] = a.x; o[1] = a.y; o[2] = b.x; o[3] = b.y;
+}
+// n consecutive shared elements starting at p (aligned to 4 when ALIGNED)
+template <int N, bool ALIGNED, typename T>
+__device__ __forceinline__ void ldn(const T* p, float* o) {
+  if constexpr (ALIGNED) {
+#pragma unroll
+    for (int j = 0; j < N; j += 4) ld4(p + j, o + j);
+  } else {
+#pragma unroll
+    for (int j = 0; j < N; ++j) o[j] = ldf(p + j);
+  }
+}
+__device__ __forceinline__ void st4(float* p, const float* v) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+}
+__device__ __forceinline__ void st4(__half* p, const float* v) {
+  __half2 a = __floats2half2_rn(v[0], v[1]), b = __floats2half2_rn(v[2], v[3]);
+  uint2 u;
+  u.x = *reinterpret_cast<uint32_t*>(&a);
+  u.y = *reinterpret_cast<uint32_t*>(&b);
+  *reinterpret_cast<uint2*>(p) = u;
+}
+
+template <int RD>
+struct TiledShape {
+  static constexpr int R = RD / 2;
+  static constexpr int R4 = (R + 3) / 4 * 4;  // halo in whole 4-element units
+  static constexpr int OFF = R4 - R;          // slab column of pixel 0's first tap
+  static constexpr int NV = (4 + RD - 1 + 3) / 4 * 4;  // shifted row values per quad
+};
+
+// Forward: CTA = 4 x 32 output pixels, warp iy = displacement row, lane =
+// (pixel row, quad of 4 columns); each thread accumulates its 4 pixels x RD
+// column displacements over 16-channel slabs: per channel one 4-element
+// read of in1 and NV/4 of the shifted in2 row feed 4*RD FMAs.
+constexpr int kFTH = 4, kFTW = 32, kFCK = 8;
+
+template <int RD>
+struct FwdTiled {
+  using S = TiledShape<RD>;
+  static constexpr int TR2 = kFTH + 2 * S::R;
+  static constexpr int TC2 = kFTW + 2 * S::R4;
+  static constexpr int S1 = kFTW + 4, S2 = TC2 + 4;
+  static constexpr int SL1 = kFCK * kFTH * S1, SL2 = kFCK * TR2 * S2;
+  template <typename T>
+  static constexpr size_t smem() { return sizeof(T) * 2 * (SL1 + SL2); }
+};
+
+template <typename T, int RD>
+__global__ void __launch_bounds__(32 * RD, 3)
+spatial_fwd_tiled(const T* __restrict__ in1, const T* __restrict__ in2, T* __restrict__ out,
+                  int C, int H, int W, float scale) {
+  using S = TiledShape<RD>;
+  using F = FwdTiled<RD>;
+  extern __shared__ __align__(16) uint8_t sraw[];
+  T* s1 = reinterpret_cast<T*>(sraw);
+  T* s2 = s1 + 2 * F::SL1;
+  const int b = blockIdx.z;
+  const int tiles_x = (W + kFTW - 1) / kFTW;
+  const int h0 = (blockIdx.x / tiles_x) * kFTH;
+  const int w0 = (blockIdx.x % tiles_x) * kFTW;
+  const int t = threadIdx.x;
+  const int iy = t >> 5, lane = t & 31;
+  const int q = lane & 7, py = lane >> 3;
+  const long long HW = (long long)H * W;
+  const T* i1b = in1 + (long long)b * C * HW;
+  const T* i2b = in2 + (long long)b * C * HW;
+
+  auto stage = [&](int buf, int c0) {
+    constexpr int U1 = kFTW / 4, U2 = F::TC2 / 4;
+    for (int u = t; u < kFCK * kFTH * U1; u += 32 * RD) {
+      const int ux = u % U1, row = (u / U1) % kFTH, cc = u / (U1 * kFTH);
+      const int c = c0 + cc, gy = h0 + row, gx = w0 + 4 * ux;
+      const bool v = c < C && gy < H && gx < W;
+      cp4(s1 + buf * F::SL1 + (cc * kFTH + row) * F::S1 + 4 * ux,
+          v ? i1b + c * HW + (long long)gy * W + gx : in1, v);
+    }
+    for (int u = t; u < kFCK * F::TR2 * U2; u += 32 * RD) {
+      const int ux = u % U2, row = (u / U2) % F::TR2, cc = u / (U2 * F::TR2);
+      const int c = c0 + cc, gy = h0 - S::R + row, gx = w0 - S::R4 + 4 * ux;
+      const bool v = c < C && gy >= 0 && gy < H && gx >= 0 && gx < W;
+      cp4(s2 + buf * F::SL2 + (cc * F::TR2 + row) * F::S2 + 4 * ux,
+          v ? i2b + c * HW + (long long)gy * W + gx : in2, v);
+    }
+    cp_commit();
+  };
+
+  float acc[RD][4];
+#pragma unroll
+  for (int ix = 0; ix < RD; ++ix)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[ix][i] = 0.f;
+  const int nch = (C + kFCK - 1) / kFCK;
+  stage(0, 0);
+  for (int k = 0; k < nch; ++k) {
+    if (k + 1 < nch) {
+      stage((k + 1) & 1, (k + 1) * kFCK);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    const T* a_s = s1 + (k & 1) * F::SL1 + py * F::S1 + 4 * q;
+    const T* v_s = s2 + (k & 1) * F::SL2 + (py + iy) * F::S2 + 4 * q + S::OFF;
+#pragma unroll 2
+    for (int cc = 0; cc < kFCK; ++cc) {
+      float a[4], v[S::NV];
+      ld4(a_s + cc * kFTH * F::S1, a);
+      ldn<S::NV, S::OFF % 4 == 0>(v_s + cc * F::TR2 * F::S2, v);
+#pragma unroll
+      for (int ix = 0; ix < RD; ++ix)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[ix][i] = fmaf(a[i], v[i + ix], acc[ix][i]);
+    }
+    __syncthreads();
+  }
+  const int gy = h0 + py, gx = w0 + 4 * q;
+  if (gy >= H || gx >= W) return;
+#pragma unroll
+  for (int ix = 0; ix < RD; ++ix) {
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = acc[ix][i] * scale;
+    st4(out + (((long long)b * RD + iy) * RD + ix) * HW + (long long)gy * W + gx, o);
+  }
+}
+
+// Backward (two gathers, no atomics): CTA = 8 x 32 pixels x 16 channels,
+// 128 threads = 64 pixel quads x 2 groups of 8 channels. The CTA's channel
+// slab of X (in2 for grad_in1, in1 for grad_in2) with its halo rows and
+// columns is copied once; the incoming gradients are copied one
+// displacement row at a time (RD maps, double-buffered). For displacement
+// row iy each thread holds the RD x 4 gradients of its pixels and, per
+// channel, reads one shifted X row segment: 4*RD FMAs per NV/4 reads.
+//   grad_in1[c,p] = scale * sum_d g[d,p] * in2[c,p+delta_d]
+//   grad_in2[c,q] = scale * sum_d g[d,q-delta_d] * in1[c,q-delta_d]
+constexpr int kBTH = 8, kBTW = 32, kBCK = 16;
+
+template <int RD, bool SHIFTED>
+struct BwdTiled {
+  using S = TiledShape<RD>;
+  static constexpr int XR = kBTH + 2 * S::R;
+  static constexpr int XC = kBTW + 2 * S::R4;
+  static constexpr int SX = XC + 4;
+  static constexpr int GC = SHIFTED ? XC : kBTW;
+  static constexpr int SG = GC + 4;
+  static constexpr int XSL = kBCK * XR * SX;
+  static constexpr int GSL = RD * kBTH * SG;
+  template <typename T>
+  static constexpr size_t smem() { return sizeof(T) * (XSL + 2 * GSL); }
+};
+
+template <typename T, int RD, bool SHIFTED>
+__global__ void __launch_bounds__(128)
+spatial_bwd_tiled(const T* __restrict__ gout, const T* __restrict__ X, T* __restrict__ gx,
+                  int C, int H, int W, float scale) {
+  using S = TiledShape<RD>;
+  using Bt = BwdTiled<RD, SHIFTED>;
+  extern __shared__ __align__(16) uint8_t sraw[];
+  T* Xs = reinterpret_cast<T*>(sraw);
+  T* Gs = Xs + Bt::XSL;
+  const int b = blockIdx.z;
+  const int c0 = blockIdx.y * kBCK;
+  const int tiles_x = (W + kBTW - 1) / kBTW;
+  const int h0 = (blockIdx.x / tiles_x) * kBTH;
+  const int w0 = (blockIdx.x % tiles_x) * kBTW;
+  const int t = threadIdx.x;
+  const int warp = t >> 5, lane = t & 31;
+  const int q = lane & 7, py = (warp & 1) * 4 + (lane >> 3), cg = warp >> 1;
+  const long long HW = (long long)H * W;
+  const T* gb = gout + (long long)b * RD * RD * HW;
+  const T* xb = X + (long long)b * C * HW;
+
+  {
+    constexpr int UX = Bt::XC / 4;
+    for (int u = t; u < kBCK * Bt::XR * UX; u += 128) {
+      const int ux = u % UX, row = (u / UX) % Bt::XR, cc = u / (UX * Bt::XR);
+      const int c = c0 + cc, gy = h0 - S::R + row, gxx = w0 - S::R4 + 4 * ux;
+      const bool v = c < C && gy >= 0 && gy < H && gxx >= 0 && gxx < W;
+      cp4(Xs + (cc * Bt::XR + row) * Bt::SX + 4 * ux,
+          v ? xb + c * HW + (long long)gy * W + gxx : X, v);
+    }
+  }
+  auto stage_g = [&](int buf, int iy) {
+    constexpr int UG = Bt::GC / 4;
+    // grad_in1: the gradients at the tile's pixels; grad_in2: at q - delta,
+    // i.e. rows shifted by -(iy - r) and the column halo
+    const int grow0 = SHIFTED ? h0 - (iy - S::R) : h0;
+    const int gcol0 = SHIFTED ? w0 - S::R4 : w0;
+    for (int u = t; u < RD * kBTH * UG; u += 128) {
+      const int ux = u % UG, row = (u / UG) % kBTH, ix = u / (UG * kBTH);
+      const int gy = grow0 + row, gxx = gcol0 + 4 * ux;
+      const bool v = gy >= 0 && gy < H && gxx >= 0 && gxx < W;
+      cp4(Gs + buf * Bt::GSL + (ix * kBTH + row) * Bt::SG + 4 * ux,
+          v ? gb + ((long long)iy * RD + ix) * HW + (long long)gy * W + gxx : gout, v);
+    }
+    cp_commit();
+  };
+
+  float acc[8][4];
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[cc][i] = 0.f;
+  stage_g(0, 0);  // commits the X slab with it
+  for (int iy = 0; iy < RD; ++iy) {
+    if (iy + 1 < RD) {
+      stage_g((iy + 1) & 1, iy + 1);
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncthreads();
+    float gv[RD][4];
+    const T* g_s = Gs + (iy & 1) * Bt::GSL + py * Bt::SG + 4 * q;
+#pragma unroll
+    for (int ix = 0; ix < RD; ++ix) {
+      if constexpr (SHIFTED)
+        ldn<4, false>(g_s + ix * kBTH * Bt::SG + S::R4 + S::R - ix, gv[ix]);
+      else
+        ld4(g_s + ix * kBTH * Bt::SG, gv[ix]);
+    }
+    const int xrow = SHIFTED ? py + 2 * S::R - iy : py + iy;
+    const T* x_s = Xs + ((cg * 8) * Bt::XR + xrow) * Bt::SX + 4 * q + S::OFF;
+#pragma unroll
+    for (int cc = 0; cc < 8; ++cc) {
+      float v[S::NV];
+      ldn<S::NV, S::OFF % 4 == 0>(x_s + cc * Bt::XR * Bt::SX, v);
+#pragma unroll
+      for (int ix = 0; ix < RD; ++ix)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          acc[cc][i] = fmaf(gv[ix][i], SHIFTED ? v[i + RD - 1 - ix] : v[i + ix], acc[cc][i]);
+    }
+    __syncthreads();
+  }
+  const int gy = h0 + py, gxx = w0 + 4 * q;
+  if (gy >= H || gxx >= W) return;
+#pragma unroll
+  for (int cc = 0; cc < 8; ++cc) {
+    const int c = c0 + cg * 8 + cc;
+    if (c >= C) break;
+    float o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) o[i] = acc[cc][i] * scale;
+    st4(gx + ((long long)b * C + c) * HW + (long long)gy * W + gxx, o);
+  }
+}
+
+// The tiled kernels need dilation 1, W % 4 == 0 and bases aligned to a
+// 4-element unit.
+bool tiled_ok(int W, int dil, size_t esize, std::initializer_list<const void*> ptrs) {
+  if (dil != 1 || W % 4 != 0) return false;
+  for (const void* p : ptrs)
+    if (p && reinterpret_cast<uintptr_t>(p) % (4 * esize)) return false;
+  return true;
+}
+
 template <typename T, int RD>
 bool fwd_rd(const void* in1, const void* in2, void* out, int B, int C, int H, int W, int dil,
             float scale, cudaStream_t s) {
+  if (tiled_ok(W, dil, sizeof(T), {in1, in2, out})) {
+    const size_t smem = FwdTiled<RD>::template smem<T>();
+    const int tiles = ((H + kFTH - 1) / kFTH) * ((W + kFTW - 1) / kFTW);
+    auto k = spatial_fwd_tiled<T, RD>;
+    if (!ensure_smem_attr((const void*)k, smem)) return false;
+    k<<<dim3(tiles, 1, B), 32 * RD, smem, s>>>((const T*)in1, (const T*)in2, (T*)out, C, H, W,
+                                                scale);
+    count_launch();
+    return check_launch("spatial_fwd_tiled");
+  }
   const int R = (RD / 2) * dil;
   const size_t smem = sizeof(float) * (8 * kTH * (kTW + 1) +
                                        (size_t)8 * (kTH + 2 * R) * odd_up(kTW + 2 * R));
@@ -242,6 +547,16 @@ bool fwd_rd(const void* in1, const void* in2, void* out, int B, int C, int H, in
 template <typename T, int RD, bool SHIFTED>
 bool bwd_one(const void* g, const void* X, void* gx, int B, int C, int H, int W, int dil,
              float scale, cudaStream_t s) {
+  if (tiled_ok(W, dil, sizeof(T), {g, X, gx})) {
+    const size_t smem = BwdTiled<RD, SHIFTED>::template smem<T>();
+    const int tiles = ((H + kBTH - 1) / kBTH) * ((W + kBTW - 1) / kBTW);
+    auto k = spatial_bwd_tiled<T, RD, SHIFTED>;
+    if (!ensure_smem_attr((const void*)k, smem)) return false;
+    k<<<dim3(tiles, (C + kBCK - 1) / kBCK, B), 128, smem, s>>>((const T*)g, (const T*)X, (T*)gx,
+                                                              C, H, W, scale);
+    count_launch();
+    return check_launch(SHIFTED ? "spatial_bwd_tiled_in2" : "spatial_bwd_tiled_in1");
+  }
   const int R = (RD / 2) * dil;
   const int TC2 = kTW + 2 * R;
   const int GW = SHIFTED ? TC2 : kTW;

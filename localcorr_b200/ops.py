@@ -50,7 +50,9 @@ def set_launch_timer(records):
     _timer = records
 
 
-def _timed(name, fn):
+def _timed(name, fn, nbytes=None):
+    """Run fn; with the timer installed, record (name, start, end, nbytes)
+    around it (nbytes: the call's algorithmic bytes, when the caller knows)."""
     if _timer is None:
         return fn()
     start = torch.cuda.Event(enable_timing=True)
@@ -58,7 +60,7 @@ def _timed(name, fn):
     start.record()
     res = fn()
     end.record()
-    _timer.append((name, start, end))
+    _timer.append((name, start, end, nbytes))
     return res
 
 
@@ -245,10 +247,11 @@ def spatial_forward(in1, in2, radius, dilation=1, scale=1.0) -> torch.Tensor:
     b, c, h, w = in1.shape
     rd = 2 * radius + 1
     out = torch.empty((b, rd, rd, h, w), dtype=in1.dtype, device=in1.device)
+    nbytes = (in1.numel() + in2.numel() + out.numel()) * in1.element_size()
     with torch.cuda.device(in1.device):
-        ok = lib.launchLocalCorrB200SpatialForward(
+        ok = _timed("spatial_fwd", lambda: lib.launchLocalCorrB200SpatialForward(
             in1.data_ptr(), in2.data_ptr(), out.data_ptr(), b, c, h, w, radius, dilation,
-            _dtype_code(in1), float(scale), _stream(in1))
+            _dtype_code(in1), float(scale), _stream(in1)), nbytes)
     _lib.check(ok, "spatial correlation forward", lib)
     return out
 
@@ -262,11 +265,14 @@ def spatial_backward(in1, in2, grad_out, radius, dilation=1, scale=1.0, need1=Tr
         grad_out = grad_out.to(in1.dtype)
     g1 = torch.empty_like(in1) if need1 else None
     g2 = torch.empty_like(in2) if need2 else None
+    # grad_out and the inputs read, the input gradients written
+    nbytes = (grad_out.numel() + (in1.numel() if need2 else 0) + (in2.numel() if need1 else 0)
+              + (in1.numel() if need1 else 0) + (in2.numel() if need2 else 0)) * in1.element_size()
     with torch.cuda.device(in1.device):
-        ok = lib.launchLocalCorrB200SpatialBackward(
+        ok = _timed("spatial_bwd", lambda: lib.launchLocalCorrB200SpatialBackward(
             in1.data_ptr(), in2.data_ptr(), grad_out.data_ptr(),
             g1.data_ptr() if g1 is not None else None, g2.data_ptr() if g2 is not None else None,
-            b, c, h, w, radius, dilation, _dtype_code(in1), float(scale), _stream(in1))
+            b, c, h, w, radius, dilation, _dtype_code(in1), float(scale), _stream(in1)), nbytes)
     _lib.check(ok, "spatial correlation backward", lib)
     return g1, g2
 

@@ -319,9 +319,13 @@ def test_transposes_exact(dtype):
 # spatial (PWC) correlation
 # ---------------------------------------------------------------------------
 
+# The first three are configuration-3 levels; W % 4 == 0 with dilation 1
+# takes the tiled kernels (radius 1..3 with a halo that is not a whole
+# 4-element unit included), the others the general kernels.
 SPATIAL_CASES = [(8, 196, 7, 16, 4, 1), (2, 32, 112, 256, 4, 1), (2, 96, 28, 64, 4, 1),
                  (1, 13, 11, 37, 3, 2), (1, 8, 9, 40, 2, 3), (1, 16, 10, 12, 0, 1),
-                 (1, 24, 20, 30, 6, 2)]
+                 (1, 24, 20, 30, 6, 2), (2, 20, 17, 24, 3, 1), (1, 40, 13, 20, 1, 1),
+                 (1, 12, 9, 36, 2, 1), (1, 33, 15, 44, 4, 1)]
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16], ids=["f32", "f16"])

@@ -16,6 +16,8 @@
 // image; each warp owns PPW of them, lanes split the channels. Outputs of a
 // level are staged in shared memory and written plane by plane, so the
 // [B, L, RD*RD, H, W] stores are coalesced along W.
+#include <initializer_list>
+
 #include "lc_common.cuh"
 
 namespace lcb200 {
@@ -30,9 +32,21 @@ __device__ __forceinline__ int grid_pos(int base, int k, int dil) {
   return dil == 1 ? base + k : base + dil * (k >> 1) + (k & 1);
 }
 
+// Four consecutive channels of a map row as floats (16-byte load in
+// float32, 8-byte load in float16); p is 4-element aligned.
+__device__ __forceinline__ float4 ld4g(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4g(const __half* p) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __half22float2(*reinterpret_cast<const __half2*>(&v.x));
+  const float2 b = __half22float2(*reinterpret_cast<const __half2*>(&v.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+
 // Dot products of one fmap1 row (fp32 in shared memory) with NX fmap2
 // samples of grid row y; lane-split channels, 8 columns per warp reduction.
-template <typename T>
+// V4: C % 4 == 0 and aligned rows, each lane reads 4 consecutive channels
+// per load (a warp covers 128 channels per step).
+template <typename T, bool V4>
 __device__ void dots_row(const float* __restrict__ f1q, const T* __restrict__ f2l,
                          int y, int hl, int wl, int xb, int dil, int NX, int C,
                          float* __restrict__ dst, int lane) {
@@ -55,11 +69,23 @@ __device__ void dots_row(const float* __restrict__ f1q, const T* __restrict__ f2
     float acc[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) acc[k] = 0.f;
-    for (int c = lane; c < C; c += 32) {
-      const float f = f1q[c];
+    if constexpr (V4) {
+      for (int c = 4 * lane; c < C; c += 128) {
+        const float4 f = *reinterpret_cast<const float4*>(f1q + c);
 #pragma unroll
-      for (int k = 0; k < 8; ++k)
-        if (ok[k]) acc[k] = fmaf(f, ldf(ptr[k] + c), acc[k]);
+        for (int k = 0; k < 8; ++k)
+          if (ok[k]) {
+            const float4 v = ld4g(ptr[k] + c);
+            acc[k] = fmaf(f.x, v.x, fmaf(f.y, v.y, fmaf(f.z, v.z, fmaf(f.w, v.w, acc[k]))));
+          }
+      }
+    } else {
+      for (int c = lane; c < C; c += 32) {
+        const float f = f1q[c];
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          if (ok[k]) acc[k] = fmaf(f, ldf(ptr[k] + c), acc[k]);
+      }
     }
     const float red = warp_reduce8(acc, lane);
     const int kk = k0 + ((lane >> 2) & 7);
@@ -67,7 +93,7 @@ __device__ void dots_row(const float* __restrict__ f1q, const T* __restrict__ f2
   }
 }
 
-template <typename T, typename TC, int PPW>
+template <typename T, typename TC, int PPW, bool V4>
 __global__ void __launch_bounds__(kThreads)
 corr_fwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
                      const TC* __restrict__ coords, T* __restrict__ corr,
@@ -100,7 +126,8 @@ corr_fwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
   float* rowB = rowA + NX;
   const T* f2b = fmap2p + (long long)b * g.batch_elems;
 
-  for (int lvl = 0; lvl < g.levels; ++lvl) {
+  // small problems spread the levels over blockIdx.z
+  for (int lvl = blockIdx.z; lvl < g.levels; lvl += gridDim.z) {
     const int hl = g.h[lvl], wl = g.w[lvl];
     const T* f2l = f2b + g.off[lvl];
     const float inv = 1.f / (float)(1 << lvl);
@@ -124,8 +151,8 @@ corr_fwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
       float* Bv = rowB;
       for (int iy = 0; iy < RD; ++iy) {
         const int y = yb + dil * iy;
-        if (iy == 0 || dil != 1) dots_row<T>(f1q, f2l, y, hl, wl, xb, dil, NX, C, A, lane);
-        dots_row<T>(f1q, f2l, y + 1, hl, wl, xb, dil, NX, C, Bv, lane);
+        if (iy == 0 || dil != 1) dots_row<T, V4>(f1q, f2l, y, hl, wl, xb, dil, NX, C, A, lane);
+        dots_row<T, V4>(f1q, f2l, y + 1, hl, wl, xb, dil, NX, C, Bv, lane);
         __syncwarp();
         for (int ix = lane; ix < RD; ix += 32) {
           const int k0 = (dil == 1) ? ix : 2 * ix;
@@ -148,7 +175,7 @@ corr_fwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
   }
 }
 
-template <typename T, typename TC, int PPW>
+template <typename T, typename TC, int PPW, bool V4>
 __global__ void __launch_bounds__(kThreads)
 corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
                      const TC* __restrict__ coords, const T* __restrict__ corr_grad,
@@ -233,18 +260,43 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
         }
         __syncwarp();
         const long long rowoff = (long long)y * wl;
-        for (int c = lane; c < C; c += 32) {
-          const float f1v = f1q[c];
-          float acc = 0.f;
-          for (int k = 0; k < NX; ++k) {
-            const int x = grid_pos(xb, k, dil);
-            const float gk = Gr[k];
-            if (x < 0 || x >= wl || gk == 0.f) continue;
-            const long long e = (rowoff + x) * C + c;
-            acc = fmaf(gk, ldf(f2l + e), acc);
-            atomicAdd(g2l + e, gk * f1v);
+        if constexpr (V4) {
+          // four channels per lane: one vector load of fmap2 and one 4-wide
+          // float32 reduction into its gradient per grid sample
+          for (int c = 4 * lane; c < C; c += 128) {
+            const float4 f1v = *reinterpret_cast<const float4*>(f1q + c);
+            float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int k = 0; k < NX; ++k) {
+              const int x = grid_pos(xb, k, dil);
+              const float gk = Gr[k];
+              if (x < 0 || x >= wl || gk == 0.f) continue;
+              const long long e = (rowoff + x) * C + c;
+              const float4 v = ld4g(f2l + e);
+              acc.x = fmaf(gk, v.x, acc.x); acc.y = fmaf(gk, v.y, acc.y);
+              acc.z = fmaf(gk, v.z, acc.z); acc.w = fmaf(gk, v.w, acc.w);
+              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(g2l + e),
+                           "f"(gk * f1v.x), "f"(gk * f1v.y), "f"(gk * f1v.z), "f"(gk * f1v.w)
+                           : "memory");
+            }
+            float4* fg = reinterpret_cast<float4*>(f1gq + c);
+            float4 o = *fg;
+            o.x += acc.x; o.y += acc.y; o.z += acc.z; o.w += acc.w;
+            *fg = o;
           }
-          f1gq[c] += acc;
+        } else {
+          for (int c = lane; c < C; c += 32) {
+            const float f1v = f1q[c];
+            float acc = 0.f;
+            for (int k = 0; k < NX; ++k) {
+              const int x = grid_pos(xb, k, dil);
+              const float gk = Gr[k];
+              if (x < 0 || x >= wl || gk == 0.f) continue;
+              const long long e = (rowoff + x) * C + c;
+              acc = fmaf(gk, ldf(f2l + e), acc);
+              atomicAdd(g2l + e, gk * f1v);
+            }
+            f1gq[c] += acc;
+          }
         }
         __syncwarp();
       }
@@ -268,14 +320,32 @@ size_t bwd_smem(int PG, int C, int RD, int NX) {
   return sizeof(float) * ((size_t)2 * PG * C + (size_t)RD * RD * PG + (size_t)kWarps * NX);
 }
 
+int num_sms_simt() {
+  int dev = 0, v = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  return v > 0 ? v : 1;
+}
+
+// 4-channel vector path: C % 4 == 0 and 4-element aligned map bases
+bool simt_v4(int C, size_t esize, std::initializer_list<const void*> ptrs) {
+  if (C % 4) return false;
+  for (const void* p : ptrs)
+    if (reinterpret_cast<uintptr_t>(p) % (4 * esize)) return false;
+  return true;
+}
+
 template <typename T, typename TC, int PPW>
 bool launch_fwd(const void* f1, const void* f2, const void* co, void* out, int B,
                 int H1, int W1, int C, int r, int dil, bool ymajor, float scale,
                 const PyrGeom& g, size_t smem, cudaStream_t s) {
-  auto k = corr_fwd_simt_kernel<T, TC, PPW>;
+  auto k = simt_v4(C, sizeof(T), {f1, f2}) ? corr_fwd_simt_kernel<T, TC, PPW, true>
+                                           : corr_fwd_simt_kernel<T, TC, PPW, false>;
   if (!ensure_smem_attr((const void*)k, smem)) return false;
   const int PG = kWarps * PPW;
   dim3 grid((H1 * W1 + PG - 1) / PG, B);
+  // fewer CTAs than a few per SM: one CTA per (pixel group, level)
+  if ((long long)grid.x * grid.y < 4ll * num_sms_simt()) grid.z = g.levels;
   k<<<grid, kThreads, smem, s>>>((const T*)f1, (const T*)f2, (const TC*)co, (T*)out,
                                  H1, W1, C, r, dil, ymajor, scale, g);
   count_launch();
@@ -287,7 +357,8 @@ bool launch_bwd(const void* f1, const void* f2, const void* co, const void* gout
                 void* f1g, float* f2g, int B, int H1, int W1, int C, int r, int dil,
                 bool ymajor, float scale, bool acc1, const PyrGeom& g, size_t smem,
                 cudaStream_t s) {
-  auto k = corr_bwd_simt_kernel<T, TC, PPW>;
+  auto k = simt_v4(C, sizeof(T), {f1, f2, f2g}) ? corr_bwd_simt_kernel<T, TC, PPW, true>
+                                                 : corr_bwd_simt_kernel<T, TC, PPW, false>;
   if (!ensure_smem_attr((const void*)k, smem)) return false;
   const int PG = kWarps * PPW;
   dim3 grid((H1 * W1 + PG - 1) / PG, B);
@@ -309,7 +380,10 @@ bool simt_forward(const void* f1, const void* f2, const void* co, void* out, int
   const int NX = (dil == 1) ? RD + 1 : 2 * RD;
   const size_t lim = (size_t)max_dyn_smem();
   int ppw = 4;
-  if (fwd_smem(kWarps * 4, C, RD, NX) > lim) ppw = 1;
+  // 4 pixels per warp unless that leaves fewer CTAs than a few per SM
+  if (fwd_smem(kWarps * 4, C, RD, NX) > lim ||
+      (long long)B * ((H1 * W1 + kWarps * 4 - 1) / (kWarps * 4)) < 4ll * num_sms_simt())
+    ppw = 1;
   const size_t smem = fwd_smem(kWarps * ppw, C, RD, NX);
   if (smem > lim) {
     set_error("pyramid forward: shared-memory footprint " + std::to_string(smem) +
@@ -341,7 +415,9 @@ bool simt_backward(const void* f1, const void* f2, const void* co, const void* g
   const int NX = (dil == 1) ? RD + 1 : 2 * RD;
   const size_t lim = (size_t)max_dyn_smem();
   int ppw = 4;
-  if (bwd_smem(kWarps * 4, C, RD, NX) > lim) ppw = 1;
+  if (bwd_smem(kWarps * 4, C, RD, NX) > lim ||
+      (long long)B * ((H1 * W1 + kWarps * 4 - 1) / (kWarps * 4)) < 4ll * num_sms_simt())
+    ppw = 1;
   const size_t smem = bwd_smem(kWarps * ppw, C, RD, NX);
   if (smem > lim) {
     set_error("pyramid backward: shared-memory footprint " + std::to_string(smem) +

@@ -143,6 +143,37 @@ LCB200_API bool launchLocalCorrB200PyramidBackwardMapDims(
     int accumulate, int engine, void* workspace, size_t workspace_bytes,
     cudaStream_t stream);
 
+/* ---- Sort reuse between a forward and its backward (no reference
+ * counterpart: the reference has no per-call state) -------------------------
+ * The tensor-core engine sorts the pixels by where their windows land before
+ * every forward and every backward. A training step runs the backward of each
+ * lookup with the coordinates of its forward, so the sort can be made once:
+ * ...ForwardKeepSort writes it to a caller buffer (sort_state, at least
+ * localCorrB200PyramidSortStateBytes() bytes, a few MB per lookup) and the
+ * matching ...BackwardWithSort reads it instead of sorting again. Arguments
+ * are those of the ...MapDims calls; `workspace` then needs only
+ * localCorrB200PyramidWorkspaceBytesMapDims() - SortStateBytes() bytes
+ * (the sort state is not part of it). The backward must get the same coords,
+ * geometry and engine as the forward that filled sort_state, and sort_state
+ * must be left untouched in between. When the configuration runs on the
+ * CUDA-core engine SortStateBytes() is 0 and sort_state is ignored. */
+LCB200_API size_t localCorrB200PyramidSortStateBytes(
+    int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int dilation, int dtype, int engine);
+LCB200_API bool launchLocalCorrB200PyramidForwardKeepSort(
+    const void* fmap1, const void* fmap2_packed, const void* coords, void* corr,
+    int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int dilation, int dtype, int coords_dtype, bool ymajor, float scale,
+    int engine, void* sort_state, size_t sort_state_bytes, void* workspace,
+    size_t workspace_bytes, cudaStream_t stream);
+LCB200_API bool launchLocalCorrB200PyramidBackwardWithSort(
+    const void* fmap1, const void* fmap2_packed, const void* coords,
+    const void* corr_grad, void* fmap1_grad, float* fmap2_grad_f32,
+    int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int dilation, int dtype, int coords_dtype, bool ymajor, float scale,
+    int accumulate, int engine, const void* sort_state, size_t sort_state_bytes,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* ---- Allocation-free forward (no counterpart in the reference) -------------
  * Some callers may not allocate device memory at the time they run the
  * correlation: a TensorRT plugin's enqueue (the engine's memory is fixed when

@@ -67,6 +67,21 @@ PROTOTYPES = {
         + [_c_int] * 9
         + [_c_int, _c_int, _c_bool, _c_float, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p],
     ),
+    "localCorrB200PyramidSortStateBytes": (_c_size_t, [_c_int] * 11),
+    "launchLocalCorrB200PyramidForwardKeepSort": (
+        _c_bool,
+        [_c_void_p] * 4
+        + [_c_int] * 9
+        + [_c_int, _c_int, _c_bool, _c_float, _c_int, _c_void_p, _c_size_t, _c_void_p,
+           _c_size_t, _c_void_p],
+    ),
+    "launchLocalCorrB200PyramidBackwardWithSort": (
+        _c_bool,
+        [_c_void_p] * 6
+        + [_c_int] * 9
+        + [_c_int, _c_int, _c_bool, _c_float, _c_int, _c_int, _c_void_p, _c_size_t, _c_void_p,
+           _c_size_t, _c_void_p],
+    ),
     "launchLocalCorrB200PyramidForwardNoAlloc": (
         _c_bool,
         [_c_void_p] * 4 + [_c_int] * 6 + [_c_int, _c_int, _c_bool, _c_float, _c_void_p],

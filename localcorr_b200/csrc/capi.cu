@@ -24,10 +24,12 @@ size_t tc_workspace_bytes(int B, int H1, int W1, int H2, int W2, int C, int radi
                           bool backward);
 bool tc_forward(const void*, const void*, const void*, void*, int B, int H1, int W1, int H2,
                 int W2, int C, int radius, int levels, int cdtype, bool ymajor, float scale,
-                void*, size_t, cudaStream_t);
+                void* sort_ws, void*, size_t, cudaStream_t);
 bool tc_backward(const void*, const void*, const void*, const void*, void*, float*, int B,
                  int H1, int W1, int H2, int W2, int C, int radius, int levels, int cdtype,
-                 bool ymajor, float scale, bool acc_f1, void*, size_t, cudaStream_t);
+                 bool ymajor, float scale, bool acc_f1, void* sort_ws, void*, size_t,
+                 cudaStream_t);
+size_t tc_sort_state_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels);
 bool tc_bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
                      int dilation, int dtype, std::string* why);
 int tc_device_status(bool reset);
@@ -245,10 +247,13 @@ bool use_tc(int engine, int B, int H1, int W1, int H2, int W2, int C, int radius
   return elig;
 }
 
+// sort_ws (tensor-core engine only, may be null): keep the pixel sort there
+// for a later backward (...KeepSort); ws then holds only the rest.
 bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1,
                      int W1, int H2, int W2, int C, int radius, int levels, int dil, int dtype, int cdtype,
                      bool ymajor, float scale, int engine, void* ws, size_t ws_bytes,
-                     bool lib_ws, cudaStream_t s) {
+                     bool lib_ws, cudaStream_t s, void* sort_ws = nullptr,
+                     size_t sort_bytes = 0) {
   clear_error();
   bool empty = false;
   if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &empty)) return false;
@@ -259,12 +264,21 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
   }
   bool ok = true;
   if (use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &ok, false, f1, f2)) {
-    const size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, false);
+    size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, false);
     if (lib_ws) {
       ScratchLease lease(need, s);
       if (!lease.ok()) return false;
       return tc_forward(f1, f2, co, out, B, H1, W1, H2, W2, C, radius, levels, cdtype, ymajor,
-                        scale, lease.ptr(), need, s);
+                        scale, nullptr, lease.ptr(), need, s);
+    }
+    if (sort_ws) {
+      const size_t sb = tc_sort_state_bytes(B, H1, W1, H2, W2, C, radius, levels);
+      if (sort_bytes < sb) {
+        set_error("sort state too small: need " + std::to_string(sb) + " B, got " +
+                  std::to_string(sort_bytes));
+        return false;
+      }
+      need -= sb;
     }
     if (ws_bytes < need || (need && ws == nullptr)) {
       set_error("workspace too small: need " + std::to_string(need) + " B, got " +
@@ -272,19 +286,21 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
       return false;
     }
     return tc_forward(f1, f2, co, out, B, H1, W1, H2, W2, C, radius, levels, cdtype, ymajor,
-                      scale, ws, ws_bytes, s);
+                      scale, sort_ws, ws, ws_bytes, s);
   }
   if (!ok) return false;
   return simt_forward(f1, f2, co, out, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, cdtype,
                       ymajor, scale, s);
 }
 
+// sort_ws (tensor-core engine only, may be null): the sort a ...KeepSort
+// forward of the same coords left there; ws then holds only the rest.
 bool pyramid_backward(const void* f1, const void* f2, const void* co, const void* gout,
                       void* f1g, float* f2g, int B, int H1, int W1, int H2, int W2, int C,
                       int radius,
                       int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
                       int accumulate, int engine, void* ws, size_t ws_bytes, bool lib_ws,
-                      cudaStream_t s) {
+                      cudaStream_t s, const void* sort_ws = nullptr, size_t sort_bytes = 0) {
   clear_error();
   bool empty = false;
   if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &empty)) return false;
@@ -301,12 +317,21 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
   }
   bool ok = true;
   if (use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &ok, true, f1, f2)) {
-    const size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, true);
+    size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, true);
     if (lib_ws) {
       ScratchLease lease(need, s);
       if (!lease.ok()) return false;
       return tc_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels,
-                         cdtype, ymajor, scale, acc1, lease.ptr(), need, s);
+                         cdtype, ymajor, scale, acc1, nullptr, lease.ptr(), need, s);
+    }
+    if (sort_ws) {
+      const size_t sb = tc_sort_state_bytes(B, H1, W1, H2, W2, C, radius, levels);
+      if (sort_bytes < sb) {
+        set_error("sort state too small: need " + std::to_string(sb) + " B, got " +
+                  std::to_string(sort_bytes));
+        return false;
+      }
+      need -= sb;
     }
     if (ws_bytes < need || (need && ws == nullptr)) {
       set_error("workspace too small: need " + std::to_string(need) + " B, got " +
@@ -314,7 +339,7 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
       return false;
     }
     return tc_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels, cdtype,
-                       ymajor, scale, acc1, ws, ws_bytes, s);
+                       ymajor, scale, acc1, const_cast<void*>(sort_ws), ws, ws_bytes, s);
   }
   if (!ok) return false;
   return simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels, dil,
@@ -376,6 +401,42 @@ size_t localCorrB200PyramidWorkspaceBytesMapDims(int B, int H1, int W1, int H2, 
       use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &ok, true);
   if (!f && !b) return 0;
   return tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, b);
+}
+
+size_t localCorrB200PyramidSortStateBytes(int B, int H1, int W1, int H2, int W2, int C,
+                                          int radius, int levels, int dilation, int dtype,
+                                          int engine) {
+  bool empty = false;
+  clear_error();
+  if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &empty) || empty)
+    return 0;
+  bool ok = true;
+  // the backward's eligibility: a sort is only kept for a tensor-core pair
+  if (!use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &ok, true))
+    return 0;
+  return tc_sort_state_bytes(B, H1, W1, H2, W2, C, radius, levels);
+}
+
+bool launchLocalCorrB200PyramidForwardKeepSort(
+    const void* fmap1, const void* fmap2_packed, const void* coords, void* corr, int B, int H1,
+    int W1, int H2, int W2, int C, int radius, int levels, int dilation, int dtype,
+    int coords_dtype, bool ymajor, float scale, int engine, void* sort_state,
+    size_t sort_state_bytes, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return pyramid_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H2, W2, C, radius,
+                         levels, dilation, dtype, coords_dtype, ymajor, scale, engine, workspace,
+                         workspace_bytes, false, stream, sort_state, sort_state_bytes);
+}
+
+bool launchLocalCorrB200PyramidBackwardWithSort(
+    const void* fmap1, const void* fmap2_packed, const void* coords, const void* corr_grad,
+    void* fmap1_grad, float* fmap2_grad_f32, int B, int H1, int W1, int H2, int W2, int C,
+    int radius, int levels, int dilation, int dtype, int coords_dtype, bool ymajor, float scale,
+    int accumulate, int engine, const void* sort_state, size_t sort_state_bytes,
+    void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  return pyramid_backward(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, fmap2_grad_f32, B,
+                          H1, W1, H2, W2, C, radius, levels, dilation, dtype, coords_dtype,
+                          ymajor, scale, accumulate, engine, workspace, workspace_bytes, false,
+                          stream, sort_state, sort_state_bytes);
 }
 
 size_t localCorrB200PyramidWorkspaceBytes(int B, int H1, int W1, int C, int radius, int levels,

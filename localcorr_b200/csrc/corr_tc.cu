@@ -1671,10 +1671,16 @@ int num_sms() {
   return v > 0 ? v : 1;
 }
 
+// Workspace regions, in one offset space: the sort state [0, sort_total)
+// (bin offsets, sorted pixel ids, inverse permutation, chunk work list) that
+// a backward can reuse from its forward, then the per-call scratch. With one
+// buffer both parts are contiguous; the ...KeepSort / ...WithSort entry
+// points put the sort state in a buffer of its own.
 struct WsLayout {
   size_t counts, offsets, keyrank, sorted, inv, work, work_count, cellpre, bsum, sbase, scratch,
       gsh, f1s;
-  size_t fwd_total, total;  // bytes the forward / the backward need
+  size_t sort_total;        // bytes of the sort state
+  size_t fwd_total, total;  // bytes the forward / the backward need (both parts)
   long long max_work;
 };
 
@@ -1685,13 +1691,14 @@ WsLayout ws_layout(const TcGeom& g) {
   size_t o = 0;
   const size_t ncells = (size_t)g.B * g.ncell;
   w.max_work = (g.npix + kTile - 1) / kTile + (long long)ncells;
-  w.counts = o; o = align256(o + ncells * kColBins * 4);
   w.offsets = o; o = align256(o + (ncells * kColBins + 1) * 4);
-  w.keyrank = o; o = align256(o + (size_t)g.npix * 8);
   w.sorted = o; o = align256(o + (size_t)g.npix * 4);
   w.inv = o; o = align256(o + (size_t)g.npix * 4);
   w.work = o; o = align256(o + (size_t)w.max_work * 16);
   w.work_count = o; o = align256(o + 4);
+  w.sort_total = o;
+  w.counts = o; o = align256(o + ncells * kColBins * 4);
+  w.keyrank = o; o = align256(o + (size_t)g.npix * 8);
   w.cellpre = o; o = align256(o + ncells * 8);
   w.bsum = o; o = align256(o + (ncells + kScanBlock - 1) / kScanBlock * 8);
   w.sbase = o; o = align256(o + (size_t)g.L * g.npix * 4);
@@ -1720,16 +1727,22 @@ struct TcWs {
   __half* f1s;
 };
 
-TcWs ws_pointers(void* ws, const WsLayout& L) {
-  uint8_t* w = static_cast<uint8_t*>(ws);
+// sort_ws: the sort state (or nullptr: it is the first sort_total bytes of
+// ws, the single-buffer layout); ws: the rest.
+TcWs ws_pointers(void* sort_ws, void* ws, const WsLayout& L) {
+  uint8_t* st = static_cast<uint8_t*>(sort_ws ? sort_ws : ws);
+  // regions past the sort state sit at (their offset - sort_total) in a
+  // separate rest buffer
+  const uintptr_t wb = reinterpret_cast<uintptr_t>(ws) - (sort_ws ? L.sort_total : 0);
+  uint8_t* w = reinterpret_cast<uint8_t*>(wb);
   TcWs p;
+  p.offsets = reinterpret_cast<int*>(st + L.offsets);
+  p.sorted = reinterpret_cast<int*>(st + L.sorted);
+  p.inv = reinterpret_cast<int*>(st + L.inv);
+  p.work = reinterpret_cast<int4*>(st + L.work);
+  p.work_count = reinterpret_cast<int*>(st + L.work_count);
   p.counts = reinterpret_cast<int*>(w + L.counts);
-  p.offsets = reinterpret_cast<int*>(w + L.offsets);
   p.keyrank = reinterpret_cast<int2*>(w + L.keyrank);
-  p.sorted = reinterpret_cast<int*>(w + L.sorted);
-  p.inv = reinterpret_cast<int*>(w + L.inv);
-  p.work = reinterpret_cast<int4*>(w + L.work);
-  p.work_count = reinterpret_cast<int*>(w + L.work_count);
   p.cellpre = reinterpret_cast<int2*>(w + L.cellpre);
   p.bsum = reinterpret_cast<int2*>(w + L.bsum);
   p.sbase = reinterpret_cast<int*>(w + L.sbase);
@@ -1842,9 +1855,17 @@ size_t tc_workspace_bytes(int B, int H1, int W1, int H2, int W2, int C, int radi
   return backward ? L.total : L.fwd_total;
 }
 
+size_t tc_sort_state_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels) {
+  TcGeom g;
+  if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, nullptr)) return 0;
+  return ws_layout(g).sort_total;
+}
+
+// sort_ws == nullptr: ws holds the whole workspace (sort state first);
+// otherwise sort_ws receives the sort state and ws holds the rest.
 bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1, int W1,
-                int H2, int W2, int C, int radius, int levels, int cdtype, bool ymajor, float scale, void* ws,
-                size_t ws_bytes, cudaStream_t s) {
+                int H2, int W2, int C, int radius, int levels, int cdtype, bool ymajor, float scale,
+                void* sort_ws, void* ws, size_t ws_bytes, cudaStream_t s) {
   TcGeom g;
   int nst = 0, nsb = 0;
   std::string why;
@@ -1853,7 +1874,7 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
     return false;
   }
   const WsLayout L = ws_layout(g);
-  if (ws_bytes < L.fwd_total) {
+  if (ws_bytes < L.fwd_total - (sort_ws ? L.sort_total : 0)) {
     set_error("tensor-core forward: workspace too small");
     return false;
   }
@@ -1862,7 +1883,7 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
     set_error("cuTensorMapEncodeTiled unavailable from the driver");
     return false;
   }
-  TcWs W = ws_pointers(ws, L);
+  TcWs W = ws_pointers(sort_ws, ws, L);
   if (!tc_sort(W, g, co, cdtype, s)) return false;
   int* sorted = W.sorted;
   int* inv = W.inv;
@@ -2016,10 +2037,13 @@ bool tc_bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, i
                       nullptr);
 }
 
+// sort_ws == nullptr: sort the coords into ws (single-buffer layout);
+// otherwise sort_ws holds the sort a forward made of the same coords and
+// geometry (tc_forward with that buffer) and ws holds the rest.
 bool tc_backward(const void* f1, const void* f2, const void* co, const void* gout, void* f1g,
                  float* f2g, int B, int H1, int W1, int H2, int W2, int C, int radius,
-                 int levels, int cdtype, bool ymajor, float scale, bool acc_f1, void* ws,
-                 size_t ws_bytes, cudaStream_t s) {
+                 int levels, int cdtype, bool ymajor, float scale, bool acc_f1, void* sort_ws,
+                 void* ws, size_t ws_bytes, cudaStream_t s) {
   TcGeom g;
   int n1 = 0, n2 = 0;
   std::string why;
@@ -2028,7 +2052,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
     return false;
   }
   const WsLayout L = ws_layout(g);
-  if (ws_bytes < L.total) {
+  if (ws_bytes < L.total - (sort_ws ? L.sort_total : 0)) {
     set_error("tensor-core backward: workspace too small");
     return false;
   }
@@ -2037,8 +2061,8 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
     set_error("cuTensorMapEncodeTiled unavailable from the driver");
     return false;
   }
-  TcWs W = ws_pointers(ws, L);
-  if (!tc_sort(W, g, co, cdtype, s)) return false;
+  TcWs W = ws_pointers(sort_ws, ws, L);
+  if (!sort_ws && !tc_sort(W, g, co, cdtype, s)) return false;
   {
     const int rows_per_block = 8 * kGatherRows;
     const long long nb = (g.npix + rows_per_block - 1) / rows_per_block;
@@ -2194,5 +2218,6 @@ extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
   void* ws = noalloc_scratch_ptr();
   if (!ws) return false;
   return tc_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H1, W1, C, radius, levels,
-                    coords_dtype, ymajor, scale, ws, LCB200_NOALLOC_SCRATCH_BYTES, stream);
+                    coords_dtype, ymajor, scale, nullptr, ws, LCB200_NOALLOC_SCRATCH_BYTES,
+                    stream);
 }

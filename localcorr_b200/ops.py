@@ -145,6 +145,17 @@ def workspace_bytes(b, h, w, c, radius, levels, dilation, dtype_code, engine,
                                                       dtype_code, engine))
 
 
+def sort_state_bytes(fmap1, fmap2_packed, radius, levels, dilation=1, engine=_lib.ENGINE_AUTO,
+                     map_hw=None) -> int:
+    """Bytes of the pixel-sort state a forward can keep for its backward
+    (``localCorrB200PyramidSortStateBytes``; 0 on the CUDA-core engine)."""
+    lib = _lib.require_library()
+    b, h, w, c = fmap1.shape
+    md = _map_dims(fmap1, fmap2_packed, levels, map_hw) or (h, w)
+    return int(lib.localCorrB200PyramidSortStateBytes(b, h, w, md[0], md[1], c, radius, levels,
+                                                      dilation, _dtype_code(fmap1), engine))
+
+
 def _map_dims(fmap1, fmap2_packed, levels, map_hw):
     """(H2, W2) of the map behind fmap2_packed, or None when it is fmap1's grid.
 
@@ -171,11 +182,14 @@ def _workspace(t: torch.Tensor, nbytes: int):
 
 def pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation=1,
                          ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO,
-                         map_hw=None) -> torch.Tensor:
+                         map_hw=None, sort_state=None) -> torch.Tensor:
     """corr [B, L, RD^2, H, W] = scale * local correlation (extended C ABI).
 
     ``map_hw=(H2, W2)``: fmap2_packed is the pyramid of an H2 x W2 map while
-    fmap1/coords/corr cover an H x W pixel grid (``...MapDims`` entry)."""
+    fmap1/coords/corr cover an H x W pixel grid (``...MapDims`` entry).
+    ``sort_state``: a uint8 tensor of :func:`sort_state_bytes` bytes that
+    receives the pixel sort for the backward of the same coords
+    (``...ForwardKeepSort`` entry)."""
     lib = _lib.require_library()
     b, h, w, c = fmap1.shape
     rd = 2 * radius + 1
@@ -184,6 +198,17 @@ def pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation=1
     md = _map_dims(fmap1, fmap2_packed, levels, map_hw)
     corr = torch.empty((b, levels, rd * rd, h, w), dtype=fmap1.dtype, device=fmap1.device)
     nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine, md)
+    if sort_state is not None:
+        md2 = md or (h, w)
+        ws, nws = _workspace(fmap1, nbytes - sort_state.numel())
+        with torch.cuda.device(fmap1.device):
+            ok = _timed("pyramid_fwd", lambda: lib.launchLocalCorrB200PyramidForwardKeepSort(
+                fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr.data_ptr(),
+                b, h, w, md2[0], md2[1], c, radius, levels, dilation, dt, cdt, bool(ymajor),
+                float(scale), engine, sort_state.data_ptr(), sort_state.numel(),
+                ws.data_ptr() if ws is not None else None, nws, _stream(fmap1)))
+        _lib.check(ok, "pyramid correlation forward", lib)
+        return corr
     ws, nws = _workspace(fmap1, nbytes)
     wsp = ws.data_ptr() if ws is not None else None
     with torch.cuda.device(fmap1.device):
@@ -203,12 +228,14 @@ def pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation=1
 
 def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels,
                           dilation=1, ymajor=False, scale=1.0, engine=_lib.ENGINE_AUTO,
-                          out=None, accumulate=0, map_hw=None):
+                          out=None, accumulate=0, map_hw=None, sort_state=None):
     """Returns (grad_fmap1 [B,H,W,C] dtype, grad_fmap2_packed float32).
 
     With ``out=(g1, g2)`` the gradients go into those buffers; ``accumulate``
     (flags ``_lib.ACC_FMAP1`` / ``_lib.ACC_FMAP2``) adds into them instead of
-    overwriting. ``map_hw`` as in :func:`pyramid_corr_forward`."""
+    overwriting. ``map_hw`` as in :func:`pyramid_corr_forward`.
+    ``sort_state``: the buffer a :func:`pyramid_corr_forward` of the same
+    coords filled (``...BackwardWithSort`` entry: no second sort)."""
     lib = _lib.require_library()
     b, h, w, c = fmap1.shape
     dt = _dtype_code(fmap1)
@@ -223,6 +250,18 @@ def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels
         g1 = torch.empty_like(fmap1)
         g2 = torch.empty(fmap2_packed.shape, dtype=torch.float32, device=fmap1.device)
     nbytes = workspace_bytes(b, h, w, c, radius, levels, dilation, dt, engine, md)
+    if sort_state is not None:
+        md2 = md or (h, w)
+        ws, nws = _workspace(fmap1, nbytes - sort_state.numel())
+        with torch.cuda.device(fmap1.device):
+            ok = _timed("pyramid_bwd", lambda: lib.launchLocalCorrB200PyramidBackwardWithSort(
+                fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(),
+                corr_grad.data_ptr(), g1.data_ptr(), g2.data_ptr(), b, h, w, md2[0], md2[1], c,
+                radius, levels, dilation, dt, cdt, bool(ymajor), float(scale), int(accumulate),
+                engine, sort_state.data_ptr(), sort_state.numel(),
+                ws.data_ptr() if ws is not None else None, nws, _stream(fmap1)))
+        _lib.check(ok, "pyramid correlation backward", lib)
+        return g1, g2
     ws, nws = _workspace(fmap1, nbytes)
     wsp = ws.data_ptr() if ws is not None else None
     with torch.cuda.device(fmap1.device):
@@ -408,10 +447,15 @@ class PyramidLookup(torch.autograd.Function):
     @staticmethod
     def forward(ctx, token, coords, state, radius, levels, scale):
         coords = coords.contiguous()
+        # The backward reuses this forward's pixel sort (tensor-core engine).
+        nb = sort_state_bytes(state.fmap1, state.fmap2_packed, radius, levels)
+        sort_state = (torch.empty(nb, dtype=torch.uint8, device=coords.device)
+                      if nb else None)
         corr = pyramid_corr_forward(state.fmap1, state.fmap2_packed, coords, radius, levels,
-                                    1, False, scale)
+                                    1, False, scale, sort_state=sort_state)
         ctx.save_for_backward(coords)
         ctx.state = state
+        ctx.sort_state = sort_state
         ctx.params = (int(radius), int(levels), float(scale))
         return corr
 
@@ -422,7 +466,9 @@ class PyramidLookup(torch.autograd.Function):
         radius, levels, scale = ctx.params
         g1, g2, flags = st.buffers()
         pyramid_corr_backward(st.fmap1, st.fmap2_packed, coords, corr_grad, radius, levels,
-                              1, False, scale, out=(g1, g2), accumulate=flags)
+                              1, False, scale, out=(g1, g2), accumulate=flags,
+                              sort_state=ctx.sort_state)
+        ctx.sort_state = None
         gc = torch.zeros_like(coords) if ctx.needs_input_grad[1] else None
         return corr_grad.new_zeros(()), gc, None, None, None, None
 

@@ -250,3 +250,56 @@ def test_reference_abi_scratch_alternating_streams():
         ref = oracle.pyramid_corr(f1.float(), f2.float(), co16.float(), 4, 4)
         s = 1.0 / math.sqrt(c)
         torch.testing.assert_close(out.double().cpu() * s, ref * s, **F16TOL)
+
+
+def test_backward_reuses_the_forward_sort():
+    # ...ForwardKeepSort leaves the pixel sort in a caller buffer and
+    # ...BackwardWithSort uses it instead of sorting again: same outputs and
+    # gradients as the self-sorting calls (grad_fmap2 up to the float32
+    # order of the reductions), five fewer launches in the backward.
+    lib = _lib.load_library()
+    b, c, h, w, levels, r = 2, 256, 40, 52, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "gauss_oob", seed=21)
+    cod = co.half().to(DEV)
+    nb = ops.sort_state_bytes(fm1, packed, r, levels, engine=_lib.ENGINE_TC)
+    assert 0 < nb < 16 << 20
+    ss = torch.empty(nb, dtype=torch.uint8, device=DEV)
+    out_k = ops.pyramid_corr_forward(fm1, packed, cod, r, levels, 1, False, 0.0625,
+                                     _lib.ENGINE_TC, sort_state=ss)
+    out_r = ops.pyramid_corr_forward(fm1, packed, cod, r, levels, 1, False, 0.0625,
+                                     _lib.ENGINE_TC)
+    assert torch.equal(out_k, out_r)
+    gout = torch.randn(out_r.shape, generator=torch.Generator().manual_seed(22)).half().to(DEV)
+    torch.cuda.synchronize()
+    lib.localCorrB200LaunchCount(1)
+    g1a, g2a = ops.pyramid_corr_backward(fm1, packed, cod, gout, r, levels, 1, False, 0.0625,
+                                         _lib.ENGINE_TC, sort_state=ss)
+    n_with = lib.localCorrB200LaunchCount(1)
+    g1b, g2b = ops.pyramid_corr_backward(fm1, packed, cod, gout, r, levels, 1, False, 0.0625,
+                                         _lib.ENGINE_TC)
+    n_without = lib.localCorrB200LaunchCount(1)
+    torch.cuda.synchronize()
+    assert n_without - n_with == 5
+    assert torch.equal(g1a, g1b)
+    torch.testing.assert_close(g2a, g2b, rtol=1e-5, atol=1e-5)
+    # and against the oracle
+    x1 = f1.double().requires_grad_(True)
+    x2 = f2.double().requires_grad_(True)
+    o = oracle.pyramid_corr(x1, x2, co.half().double(), levels, r) * 0.0625
+    e1, e2 = torch.autograd.grad(o, [x1, x2], gout.double().cpu())
+    torch.testing.assert_close(g1a.permute(0, 3, 1, 2).double().cpu(), e1, **F16TOL)
+    g2n = ops.pyramid_build_backward(g2a, (b, c, h, w), levels, torch.float32)
+    torch.testing.assert_close(g2n.double().cpu(), e2, **F16TOL)
+
+
+def test_sort_state_too_small_is_rejected():
+    lib = _lib.load_library()
+    b, c, h, w, levels, r = 1, 128, 24, 40, 4, 4
+    f1, f2, co, fm1, packed = _inputs(b, c, h, w, levels, "uniform8", seed=23)
+    nb = ops.sort_state_bytes(fm1, packed, r, levels, engine=_lib.ENGINE_TC)
+    ss = torch.empty(nb - 256, dtype=torch.uint8, device=DEV)
+    with pytest.raises(RuntimeError, match="sort state too small"):
+        ops.pyramid_corr_forward(fm1, packed, co.half().to(DEV), r, levels, 1, False, 1.0,
+                                 _lib.ENGINE_TC, sort_state=ss)
+    assert lib.localCorrB200PyramidSortStateBytes(1, 24, 40, 24, 40, 128, 4, 4, 1, _lib.F32,
+                                                  _lib.ENGINE_AUTO) == 0

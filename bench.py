@@ -28,6 +28,11 @@ builds its band's pyramid levels, one all-gather assembles the frame's
 pyramid on every rank (localcorr_b200.bands), and the lookups of the band run
 locally; value = the frame's lookups per second.
 
+Every workload except the row bands replays its timed steps from a CUDA
+graph captured through the public API after the warm-up (the step's work is
+unchanged; the graph removes the host launch gaps that dominate at one image
+per GPU); the per-kernel times of the roofline come from an eager pass.
+
 The reference arm (--impl reference) times the reference's CPU path as
 restated in oracle/oracle.py (the all-pairs matmul + grid_sample formulation
 of onnx_generic.py:58-156) on the host cores, on a bounded sample.
@@ -453,10 +458,17 @@ def main(argv=None):
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=None,
                     help="override the per-GPU batch (smaller cases of a workload, for profiling)")
+    ap.add_argument("--cuda-graph", choices=["auto", "on", "off"], default="auto",
+                    help="replay the timed steps from a CUDA graph (auto: the workload's default)")
     args = ap.parse_args(argv)
     cfg = dict(CONFIGS[args.config])
     if args.batch is not None:
         cfg["B"] = args.batch
+    # Timed steps replay from a CUDA graph captured through the public API,
+    # except for row bands (their step holds an NCCL all-gather).
+    cfg.setdefault("graph", not cfg.get("bands"))
+    if args.cuda_graph != "auto":
+        cfg["graph"] = args.cuda_graph == "on"
     if args.impl == "reference":
         return reference_arm(args, cfg, args.config)
 
@@ -722,6 +734,11 @@ def main(argv=None):
             "clocks": clocks,
         }
         print(json.dumps(line), flush=True)
+    # graphs go before the process group (none holds a collective, but a
+    # graph that did would keep the exit waiting)
+    if use_graph:
+        del g_main, graphed
+        torch.cuda.synchronize(device)
     if dist is not None:
         dist.barrier()
         dist.destroy_process_group()

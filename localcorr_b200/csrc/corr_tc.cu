@@ -350,6 +350,64 @@ tc_cellwrite_kernel(const int* __restrict__ counts, const int2* __restrict__ cel
     work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
 }
 
+// The whole scan in one block of 1024 threads (up to kSmallScanCpt cells per
+// thread), for small problems (one or two images), where the three-pass
+// form's launches cost more than the scan itself.
+constexpr int kSmallScanCpt = 4;
+__global__ void __launch_bounds__(1024)
+tc_scan_small_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
+                     int4* __restrict__ work, int* __restrict__ total,
+                     int* __restrict__ work_count, int ncell_total, int ncell) {
+  using Scan = cub::BlockScan<int2, 1024>;
+  __shared__ typename Scan::TempStorage tmp;
+  const int c0 = threadIdx.x * kSmallScanCpt;
+  int2 mine = make_int2(0, 0);
+#pragma unroll
+  for (int k = 0; k < kSmallScanCpt; ++k) {
+    const int i = c0 + k;
+    if (i < ncell_total) {
+      int bins[kColBins];
+      load_cell_bins(counts, i, bins);
+      int cnt = 0;
+#pragma unroll
+      for (int q = 0; q < kColBins; ++q) cnt += bins[q];
+      mine.x += cnt;
+      mine.y += (cnt + kTile - 1) / kTile;
+    }
+  }
+  int2 ex, tot;
+  Scan(tmp).ExclusiveScan(mine, ex, make_int2(0, 0), PairSum(), tot);
+  int acc = ex.x, coff = ex.y;
+  for (int k = 0; k < kSmallScanCpt; ++k) {
+    const int i = c0 + k;
+    if (i >= ncell_total) break;
+    int bins[kColBins];
+    load_cell_bins(counts, i, bins);
+    const int off = acc;
+    int4* dst = reinterpret_cast<int4*>(offsets + (long long)i * kColBins);
+#pragma unroll
+    for (int q = 0; q < kColBins / 4; ++q) {
+      int4 v;
+      v.x = acc; acc += bins[4 * q];
+      v.y = acc; acc += bins[4 * q + 1];
+      v.z = acc; acc += bins[4 * q + 2];
+      v.w = acc; acc += bins[4 * q + 3];
+      dst[q] = v;
+    }
+    const int cnt = acc - off;
+    const int nch = (cnt + kTile - 1) / kTile;
+    const int b = i / ncell;
+    const int cell = i - b * ncell;
+    for (int j = 0; j < nch; ++j)
+      work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
+    coff += nch;
+  }
+  if (threadIdx.x == 0) {
+    *total = tot.x;
+    *work_count = tot.y;
+  }
+}
+
 __global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* __restrict__ offsets,
                                   int* __restrict__ sorted, int* __restrict__ inv, TcGeom g) {
   const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
@@ -559,6 +617,12 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
         const int t = gw * 4 * GROWS + 4 * i + rr;
         rid[i] = t < n ? p.sorted[start + t] : -1;
       }
+      // Bring the rows into L2 while the previous chunk's MMAs still need
+      // the A tile (lanes 0..3 of a row: one 128-byte line per 64 channels).
+#pragma unroll
+      for (int i = 0; i < GROWS; ++i)
+        if (rid[i] >= 0 && sub < g.KC)
+          asm volatile("prefetch.global.L2 [%0];" ::"l"(p.fmap1 + (long long)rid[i] * g.C + sub * 64));
       if (!tc::mbar_wait(a_empty, (it & 1) ^ 1, abort)) break;
       for (int kc = 0; kc < g.KC; ++kc) {
 #pragma unroll
@@ -1765,6 +1829,16 @@ bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStr
   count_launch();
   if (!check_launch("tc_hist")) return false;
   const int ncells = g.B * g.ncell;
+  if (ncells <= 1024 * kSmallScanCpt) {
+    tc_scan_small_kernel<<<1, 1024, 0, s>>>(W.counts, W.offsets,
+                                             W.work, W.offsets + (size_t)ncells * kColBins,
+                                             W.work_count, ncells, g.ncell);
+    count_launch();
+    if (!check_launch("tc_scan_small")) return false;
+    tc_scatter_kernel<<<blocks, threads, 0, s>>>(W.keyrank, W.offsets, W.sorted, W.inv, g);
+    count_launch();
+    return check_launch("tc_scatter");
+  }
   const int nsb = (ncells + kScanBlock - 1) / kScanBlock;
   tc_cellscan_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, ncells);
   count_launch();

@@ -261,6 +261,28 @@ LCB200_API int localCorrB200Version(void);
  * benchmarks). */
 LCB200_API long long localCorrB200LaunchCount(int reset);
 
+/* ---- Deterministic mode ---------------------------------------------------
+ * No reference counterpart (the reference's backward adds grad_fmap2 with
+ * float atomics, cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:909-916).
+ * When on (process-wide, off by default), the tensor-core engine sorts the
+ * pixels of a lookup in a fixed order (forward and backward) and adds every
+ * grad_fmap2 position once per call, so repeated calls on the same inputs
+ * give bitwise identical results; the CUDA-core engine's backward, whose
+ * scattered float adds cannot be ordered, fails with an error instead.
+ * Set it before the forward whose sort a ...BackwardWithSort reuses. */
+LCB200_API void localCorrB200SetDeterministic(int on);
+LCB200_API int localCorrB200GetDeterministic(void);
+
+/* ---- Bounds-check build ---------------------------------------------------
+ * liblocalcorr_b200_checked.so (python -m localcorr_b200.csrc.build
+ * --bounds-check) is the same library compiled with LC_BOUNDS_CHECK: every
+ * data-dependent global index in the kernels is checked on the device, an
+ * out-of-range access is skipped and recorded, and the entry point that
+ * launched the kernel synchronises its stream and returns false with the
+ * site in localCorrB200GetLastError(). Returns the violations recorded since
+ * the last reset, or -1 in the normal build. */
+LCB200_API long long localCorrB200BoundsViolations(int reset);
+
 #ifdef __cplusplus
 }
 #endif

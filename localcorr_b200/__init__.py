@@ -28,6 +28,7 @@ from .blocks import (
 )
 from .blocks import LocalCorrCudaPyramidSpatialOnnx
 from .spatial_corr import LocalCorrCudaPyramidSampler, get_sycl_xpu_extension
+from .ops import is_deterministic, set_deterministic
 
 # The reference's Triton autograd Functions (triton/pyramid_corr.py:845-1246,
 # triton/spatial_corr.py:108-207) have no counterpart: there is no Triton
@@ -63,4 +64,6 @@ __all__ = [
     "LocalCorrTritonFused",
     "TritonSpatialCorrelationFunction",
     "TritonSpatialCorrelationSampler",
+    "set_deterministic",
+    "is_deterministic",
 ]

@@ -4,18 +4,24 @@ The library is loaded once, from the package directory, where
 ``python -m localcorr_b200.csrc.build`` (or ``__graft_entry__.build()``) puts
 it. There is no fallback: when the library is missing every CUDA op raises
 ImportError, as the reference does for its unbuilt CUDA library
-(blocks.py:552-565).
+(blocks.py:552-565). With ``LOCALCORR_B200_BOUNDS_CHECK=1`` in the
+environment the bounds-checked build (liblocalcorr_b200_checked.so, built
+with ``--bounds-check``) is loaded instead.
 """
 
 from __future__ import annotations
 
 import ctypes
 import logging
+import os
 from pathlib import Path
 
 logger = logging.getLogger(__name__)
 
-LIB_PATH = Path(__file__).resolve().parent / "liblocalcorr_b200.so"
+LIB_PATH_DEFAULT = Path(__file__).resolve().parent / "liblocalcorr_b200.so"
+LIB_PATH_CHECKED = Path(__file__).resolve().parent / "liblocalcorr_b200_checked.so"
+BOUNDS_CHECK = os.environ.get("LOCALCORR_B200_BOUNDS_CHECK", "") not in ("", "0")
+LIB_PATH = LIB_PATH_CHECKED if BOUNDS_CHECK else LIB_PATH_DEFAULT
 
 F32 = 0
 F16 = 1
@@ -108,6 +114,9 @@ PROTOTYPES = {
     "localCorrB200DeviceStatus": (_c_int, [_c_int]),
     "localCorrB200Version": (_c_int, []),
     "localCorrB200LaunchCount": (ctypes.c_longlong, [_c_int]),
+    "localCorrB200SetDeterministic": (None, [_c_int]),
+    "localCorrB200GetDeterministic": (_c_int, []),
+    "localCorrB200BoundsViolations": (ctypes.c_longlong, [_c_int]),
 }
 
 _LIB = None

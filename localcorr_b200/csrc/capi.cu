@@ -1,6 +1,8 @@
 // extern "C" entry points of liblocalcorr_b200.so (declared in
 // include/localcorr_b200.h): argument validation, engine selection and
 // error reporting around the kernels.
+#include <nvtx3/nvToolsExt.h>
+
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -48,7 +50,78 @@ thread_local std::string g_last_error;
 // every host thread's launches (autograd runs backward passes on its own
 // worker threads)
 std::atomic<long long> g_launches{0};
+std::atomic<int> g_deterministic{0};
 }  // namespace
+
+// NVTX range around an entry point's host work and launches (shows up in
+// Nsight Systems / ncu --nvtx; free when no tool is attached).
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
+
+bool deterministic_mode() { return g_deterministic.load(std::memory_order_relaxed) != 0; }
+
+bool bounds_read_tc(unsigned long long out[3], bool reset);
+bool bounds_read_simt(unsigned long long out[3], bool reset);
+bool bounds_read_spatial(unsigned long long out[3], bool reset);
+
+namespace {
+std::atomic<long long> g_bounds_total{0};
+const char* const kSiteNames[kSiteCount] = {
+    "none",
+    "tc_hist (sort bin)",
+    "tc_scatter (sorted position)",
+    "tc_rank_fix (bin member)",
+    "tc_gather_rows (fmap1 row)",
+    "tc_fwd (chunk range)",
+    "tc_fwd (member pixel)",
+    "tc_unsort (sorted position)",
+    "tc_gint (sorted position)",
+    "tc_bwd1 (pixel)",
+    "tc_bwd2 (candidate position)",
+    "simt forward (fmap2 element)",
+    "simt backward (fmap2 element)",
+    "spatial (in2 element)",
+};
+}  // namespace
+
+bool bounds_finish(bool ok, cudaStream_t s) {
+#ifdef LC_BOUNDS_CHECK
+  if (!ok) return false;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess) return check_launch("bounds check");
+  if (cs != cudaStreamCaptureStatusNone) return true;  // nothing has run yet
+  if (cudaStreamSynchronize(s) != cudaSuccess) return check_launch("bounds check");
+  unsigned long long total = 0, site = 0, idx = 0;
+  for (auto rd : {bounds_read_tc, bounds_read_simt, bounds_read_spatial}) {
+    unsigned long long r[3];
+    if (!rd(r, true)) return check_launch("bounds check: reading the device record");
+    if (r[0] && !total) { site = r[1]; idx = r[2]; }
+    total += r[0];
+  }
+  if (!total) return true;
+  g_bounds_total.fetch_add((long long)total);
+  set_error("bounds check: " + std::to_string(total) + " out-of-range index(es), first at " +
+            (site < (unsigned long long)kSiteCount ? kSiteNames[site] : "?") + ", index " +
+            std::to_string((long long)idx));
+  return false;
+#else
+  (void)s;
+  return ok;
+#endif
+}
+
+long long bounds_total(bool reset) {
+#ifdef LC_BOUNDS_CHECK
+  return reset ? g_bounds_total.exchange(0) : g_bounds_total.load();
+#else
+  (void)reset;
+  return -1;
+#endif
+}
 
 void set_error(const std::string& msg) { g_last_error = msg; }
 void clear_error() { g_last_error.clear(); }
@@ -249,11 +322,11 @@ bool use_tc(int engine, int B, int H1, int W1, int H2, int W2, int C, int radius
 
 // sort_ws (tensor-core engine only, may be null): keep the pixel sort there
 // for a later backward (...KeepSort); ws then holds only the rest.
-bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1,
-                     int W1, int H2, int W2, int C, int radius, int levels, int dil, int dtype, int cdtype,
-                     bool ymajor, float scale, int engine, void* ws, size_t ws_bytes,
-                     bool lib_ws, cudaStream_t s, void* sort_ws = nullptr,
-                     size_t sort_bytes = 0) {
+bool pyramid_forward_impl(const void* f1, const void* f2, const void* co, void* out, int B,
+                          int H1, int W1, int H2, int W2, int C, int radius, int levels, int dil,
+                          int dtype, int cdtype, bool ymajor, float scale, int engine, void* ws,
+                          size_t ws_bytes, bool lib_ws, cudaStream_t s, void* sort_ws,
+                          size_t sort_bytes) {
   clear_error();
   bool empty = false;
   if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &empty)) return false;
@@ -295,12 +368,11 @@ bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, 
 
 // sort_ws (tensor-core engine only, may be null): the sort a ...KeepSort
 // forward of the same coords left there; ws then holds only the rest.
-bool pyramid_backward(const void* f1, const void* f2, const void* co, const void* gout,
-                      void* f1g, float* f2g, int B, int H1, int W1, int H2, int W2, int C,
-                      int radius,
-                      int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
-                      int accumulate, int engine, void* ws, size_t ws_bytes, bool lib_ws,
-                      cudaStream_t s, const void* sort_ws = nullptr, size_t sort_bytes = 0) {
+bool pyramid_backward_impl(const void* f1, const void* f2, const void* co, const void* gout,
+                           void* f1g, float* f2g, int B, int H1, int W1, int H2, int W2, int C,
+                           int radius, int levels, int dil, int dtype, int cdtype, bool ymajor,
+                           float scale, int accumulate, int engine, void* ws, size_t ws_bytes,
+                           bool lib_ws, cudaStream_t s, const void* sort_ws, size_t sort_bytes) {
   clear_error();
   bool empty = false;
   if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, dil, dtype, &empty)) return false;
@@ -342,8 +414,41 @@ bool pyramid_backward(const void* f1, const void* f2, const void* co, const void
                        ymajor, scale, acc1, const_cast<void*>(sort_ws), ws, ws_bytes, s);
   }
   if (!ok) return false;
+  if (deterministic_mode()) {
+    set_error("deterministic mode: the CUDA-core engine adds grad_fmap2 with float atomics; "
+              "only the tensor-core engine (float16 maps, dilation 1, 1..4 levels, C in "
+              "{64,128,192,256}, radius 3/4/8) has a deterministic backward");
+    return false;
+  }
   return simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels, dil,
                        dtype, cdtype, ymajor, scale, acc1, s);
+}
+
+bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1,
+                     int W1, int H2, int W2, int C, int radius, int levels, int dil, int dtype,
+                     int cdtype, bool ymajor, float scale, int engine, void* ws, size_t ws_bytes,
+                     bool lib_ws, cudaStream_t s, void* sort_ws = nullptr,
+                     size_t sort_bytes = 0) {
+  NvtxRange range("localcorr_b200 pyramid forward");
+  return bounds_finish(
+      pyramid_forward_impl(f1, f2, co, out, B, H1, W1, H2, W2, C, radius, levels, dil, dtype,
+                           cdtype, ymajor, scale, engine, ws, ws_bytes, lib_ws, s, sort_ws,
+                           sort_bytes),
+      s);
+}
+
+bool pyramid_backward(const void* f1, const void* f2, const void* co, const void* gout,
+                      void* f1g, float* f2g, int B, int H1, int W1, int H2, int W2, int C,
+                      int radius, int levels, int dil, int dtype, int cdtype, bool ymajor,
+                      float scale, int accumulate, int engine, void* ws, size_t ws_bytes,
+                      bool lib_ws, cudaStream_t s, const void* sort_ws = nullptr,
+                      size_t sort_bytes = 0) {
+  NvtxRange range("localcorr_b200 pyramid backward");
+  return bounds_finish(
+      pyramid_backward_impl(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels,
+                            dil, dtype, cdtype, ymajor, scale, accumulate, engine, ws, ws_bytes,
+                            lib_ws, s, sort_ws, sort_bytes),
+      s);
 }
 
 bool validate_layout(int B, int C, int H, int W, int dtype) {
@@ -498,6 +603,7 @@ bool launchLocalCorrB200PyramidBuild(const void* fmap2_nchw, void* fmap2_packed,
   bool empty = false;
   if (!validate_pyramid(B, H, W, H, W, C, 0, levels, 1, dtype, &empty)) return false;
   if (empty) return true;
+  NvtxRange range("localcorr_b200 pyramid build");
   return layout_pyramid_build(fmap2_nchw, fmap2_packed, B, C, H, W, levels, dtype, stream);
 }
 
@@ -508,6 +614,7 @@ bool launchLocalCorrB200PyramidBuildBackward(const void* grad_packed, bool grad_
   bool empty = false;
   if (!validate_pyramid(B, H, W, H, W, C, 0, levels, 1, dtype, &empty)) return false;
   if (empty) return true;
+  NvtxRange range("localcorr_b200 pyramid build backward");
   return layout_pyramid_build_grad(grad_packed, grad_is_f32, grad_fmap2_nchw, B, C, H, W,
                                    levels, dtype, stream);
 }
@@ -538,7 +645,9 @@ bool launchLocalCorrB200SpatialForward(const void* in1, const void* in2, void* o
     return false;
   }
   if (B == 0 || H == 0 || W == 0) return true;
-  return spatial_forward(in1, in2, out, B, C, H, W, radius, dilation, dtype, scale, stream);
+  NvtxRange range("localcorr_b200 spatial forward");
+  return bounds_finish(
+      spatial_forward(in1, in2, out, B, C, H, W, radius, dilation, dtype, scale, stream), stream);
 }
 
 bool launchLocalCorrB200SpatialBackward(const void* in1, const void* in2, const void* grad_out,
@@ -552,8 +661,11 @@ bool launchLocalCorrB200SpatialBackward(const void* in1, const void* in2, const 
     return false;
   }
   if (B == 0 || H == 0 || W == 0) return true;
-  return spatial_backward(in1, in2, grad_out, grad_in1, grad_in2, B, C, H, W, radius, dilation,
-                          dtype, scale, stream);
+  NvtxRange range("localcorr_b200 spatial backward");
+  return bounds_finish(
+      spatial_backward(in1, in2, grad_out, grad_in1, grad_in2, B, C, H, W, radius, dilation,
+                          dtype, scale, stream),
+      stream);
 }
 
 const char* localCorrB200GetLastError(void) { return g_last_error.c_str(); }
@@ -565,5 +677,11 @@ int localCorrB200Version(void) { return 100; }
 long long localCorrB200LaunchCount(int reset) {
   return reset ? g_launches.exchange(0) : g_launches.load();
 }
+
+void localCorrB200SetDeterministic(int on) { g_deterministic.store(on ? 1 : 0); }
+
+int localCorrB200GetDeterministic(void) { return g_deterministic.load(); }
+
+long long localCorrB200BoundsViolations(int reset) { return bounds_total(reset != 0); }
 
 }  // extern "C"

@@ -59,7 +59,10 @@ __device__ void dots_row(const float* __restrict__ f1q, const T* __restrict__ f2
     for (int k = 0; k < 8; ++k) {
       const int x = grid_pos(xb, k0 + k, dil);
       ok[k] = rowok && (k0 + k < NX) && x >= 0 && x < wl;
-      ptr[k] = f2l + ((long long)(ok[k] ? y : 0) * wl + (ok[k] ? x : 0)) * C;
+      const long long e = ((long long)(ok[k] ? y : 0) * wl + (ok[k] ? x : 0)) * C;
+      if (ok[k] && !LCB_IN(e >= 0 && e + C <= (long long)hl * wl * C, kSiteSimtFwd, e))
+        ok[k] = false;
+      ptr[k] = f2l + e;
       any |= ok[k];
     }
     if (!any) {
@@ -271,6 +274,7 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
               const float gk = Gr[k];
               if (x < 0 || x >= wl || gk == 0.f) continue;
               const long long e = (rowoff + x) * C + c;
+              if (!LCB_IN(e >= 0 && e + 4 <= (long long)hl * wl * C, kSiteSimtBwd, e)) continue;
               const float4 v = ld4g(f2l + e);
               acc.x = fmaf(gk, v.x, acc.x); acc.y = fmaf(gk, v.y, acc.y);
               acc.z = fmaf(gk, v.z, acc.z); acc.w = fmaf(gk, v.w, acc.w);
@@ -292,6 +296,7 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
               const float gk = Gr[k];
               if (x < 0 || x >= wl || gk == 0.f) continue;
               const long long e = (rowoff + x) * C + c;
+              if (!LCB_IN(e >= 0 && e < (long long)hl * wl * C, kSiteSimtBwd, e)) continue;
               acc = fmaf(gk, ldf(f2l + e), acc);
               atomicAdd(g2l + e, gk * f1v);
             }
@@ -438,5 +443,7 @@ bool simt_backward(const void* f1, const void* f2, const void* co, const void* g
   LCB_BWD(__half, __half)
 #undef LCB_BWD
 }
+
+LCB_BOUNDS_READER(bounds_read_simt)
 
 }  // namespace lcb200

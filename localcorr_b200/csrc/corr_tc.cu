@@ -43,6 +43,7 @@
 // error status, all roles wind down, TMEM is freed and the kernel returns.
 #include <cub/block/block_scan.cuh>
 #include <cudaTypedefs.h>
+#include <climits>
 
 #include <mutex>
 #include <string>
@@ -200,7 +201,9 @@ bool make_tc_geom(int B, int H, int W, int H2, int W2, int C, int r, int L, TcGe
     const int span_x = (16 + 2 * r + 1) << l;
     const int rows = span_y / kCellY + 2;
     const int cols = span_x / kCellX + 2;
-    t.rpi[l] = std::max(1, 16 / cols);
+    // Deterministic mode: one item per tile (all its cell rows), so every
+    // position gets exactly one add per call.
+    t.rpi[l] = deterministic_mode() ? rows : std::max(1, 16 / cols);
     t.qgroups[l] = ceil_div(rows, t.rpi[l]);
   }
   t.items_before[0] = 0;
@@ -248,8 +251,10 @@ __global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ 
     const int bx = (int)fx, by = (int)fy;
     const int cell = ((by - g.ylo) / kCellY) * g.ncx + (bx - g.xlo) / kCellX;
     const int key = cell * kColBins + (bx - g.xlo) % kCellX;  // (cell, column in cell)
-    kr.x = key;
-    kr.y = atomicAdd(counts + (long long)b * g.ncell * kColBins + key, 1);
+    if (LCB_IN(key >= 0 && key < g.ncell * kColBins, kSiteTcHist, key)) {
+      kr.x = key;
+      kr.y = atomicAdd(counts + (long long)b * g.ncell * kColBins + key, 1);
+    }
   }
   keyrank[gid] = kr;
 }
@@ -419,8 +424,35 @@ __global__ void tc_scatter_kernel(const int2* __restrict__ keyrank, const int* _
   }
   const int b = (int)(gid / g.HW);
   const int pos = offsets[(long long)b * g.ncell * kColBins + kr.x] + kr.y;
+  if (!LCB_IN(pos >= 0 && pos < g.npix, kSiteTcScatter, pos)) return;
   sorted[pos] = (int)gid;
   inv[gid] = pos;
+}
+
+// Deterministic order within the sort bins. The histogram's ranks come from
+// atomics, so a bin's pixels land in thread-timing order; this pass gives
+// each pixel of a bin the rank = number of the bin's pixels with a smaller
+// index (one warp per bin, bins of any size), and the scatter then runs
+// again with those ranks.
+__global__ void tc_rank_fix_kernel(const int* __restrict__ offsets, const int* __restrict__ sorted,
+                                   int2* __restrict__ keyrank, long long nbins, long long npix) {
+  const long long bin = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (bin >= nbins) return;  // warp-uniform
+  const int s0 = offsets[bin];
+  const int n = offsets[bin + 1] - s0;
+  if (n < 2) return;
+  for (int i0 = 0; i0 < n; i0 += 32) {
+    const int mine = i0 + lane < n ? sorted[s0 + i0 + lane] : INT_MAX;
+    int rank = 0;
+    for (int j0 = 0; j0 < n; j0 += 32) {
+      const int other = j0 + lane < n ? sorted[s0 + j0 + lane] : INT_MAX;
+#pragma unroll 8
+      for (int m = 0; m < 32; ++m) rank += __shfl_sync(0xffffffffu, other, m) < mine;
+    }
+    if (i0 + lane < n && LCB_IN(mine >= 0 && mine < npix, kSiteTcRankFix, mine))
+      keyrank[mine].y = rank;
+  }
 }
 
 // Sorted copy of fmap1 for the grad_fmap2 pull: row i = fmap1 row sorted[i]
@@ -442,8 +474,11 @@ __global__ void tc_gather_rows_kernel(const __half* __restrict__ fmap1, const in
   for (int k = 0; k < kGatherRows; ++k) {
     const long long row = row0 + k;
     v[k] = make_uint4(0, 0, 0, 0);
-    if (row < ns)
-      v[k] = reinterpret_cast<const uint4*>(fmap1 + (long long)sorted[row] * g.C)[lane];
+    if (row < ns) {
+      const int src = sorted[row];
+      if (LCB_IN(src >= 0 && src < g.npix, kSiteTcGather, src))
+        v[k] = reinterpret_cast<const uint4*>(fmap1 + (long long)src * g.C)[lane];
+    }
   }
 #pragma unroll
   for (int k = 0; k < kGatherRows; ++k) {
@@ -578,7 +613,8 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
         if (!tc::mbar_wait(s_full + sbuf, suse & 1, abort)) { ok = false; break; }
         const uint32_t* src = sOut + sbuf * stage_words;
         uint4* dst = reinterpret_cast<uint4*>(p.scratch + ((long long)l * g.npix + start) * RDP);
-        const int nunits = n * UPR;
+        const int nunits =
+            LCB_IN(start >= 0 && n >= 0 && start + n <= g.npix, kSiteTcFwdWork, start) ? n * UPR : 0;
         for (int u0 = ct; u0 < nunits; u0 += 4 * NCT) {
           uint4 v[4];
 #pragma unroll
@@ -616,6 +652,7 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
       for (int i = 0; i < GROWS; ++i) {
         const int t = gw * 4 * GROWS + 4 * i + rr;
         rid[i] = t < n ? p.sorted[start + t] : -1;
+        if (!LCB_IN(rid[i] >= -1 && rid[i] < g.npix, kSiteTcFwdRow, rid[i])) rid[i] = -1;
       }
       // Bring the rows into L2 while the previous chunk's MMAs still need
       // the A tile (lanes 0..3 of a row: one 128-byte line per 64 channels).
@@ -738,7 +775,8 @@ __global__ void __launch_bounds__(fwd_threads(RADIUS), 1) tc_fwd_kernel(const __
       float cx = 0.f, cy = 0.f;
       if (valid) {
         const int gid = p.sorted[start + t];
-        const int pix = gid - b * g.HW;
+        int pix = gid - b * g.HW;
+        if (!LCB_IN(pix >= 0 && pix < g.HW, kSiteTcFwdRow, gid)) pix = 0;
         if (p.coords_f32) {
           const float* co = reinterpret_cast<const float*>(p.coords) + (long long)b * 2 * g.HW + pix;
           cx = co[0]; cy = co[g.HW];
@@ -866,6 +904,7 @@ __device__ __forceinline__ void gint_tile(const __half* __restrict__ tile, uint4
   if (pix < g.HW) {
     const long long gid = (long long)b * g.HW + pix;
     idx = inv[gid];
+    if (!LCB_IN(idx >= -1 && idx < g.npix, kSiteTcGint, idx)) idx = -1;
     if (idx < 0) {
       if (l == 0 && !acc_f1) {
         uint4* row = reinterpret_cast<uint4*>(grad_f1 + gid * g.C);
@@ -1256,10 +1295,14 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
     for (int wi = blockIdx.x; wi < nwork && ok; wi += gridDim.x) {
       const int4 wk = p.work[wi];
       const int b = wk.x, cell = wk.y, start = wk.z, n = wk.w;
-      const bool valid = t < n;
       const int idx = start + t;
+      const bool valid = t < n && LCB_IN(idx >= 0 && idx < g.npix, kSiteTcBwd1, idx);
       float cx = 0.f, cy = 0.f;
-      if (valid) pixel_coords(p, b, p.sorted[idx] - b * g.HW, cx, cy);
+      if (valid) {
+        int pix = p.sorted[idx] - b * g.HW;
+        if (!LCB_IN(pix >= 0 && pix < g.HW, kSiteTcBwd1, pix)) pix = 0;
+        pixel_coords(p, b, pix, cx, cy);
+      }
       const int ccy = cell / g.ncx, ccx = cell - ccy * g.ncx;
       const int cell_y0 = g.ylo + ccy * kCellY, cell_x0 = g.xlo + ccx * kCellX;
       for (int l = 0; l < g.L && ok; ++l) {
@@ -1310,8 +1353,9 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
     for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x, ++it) {
       const int4 wk = p.work[wi];
       const int buf = it & 1;
-      const bool valid = t < wk.w;
-      const int gid = valid ? p.sorted[wk.z + t] : 0;
+      bool valid = t < wk.w;
+      int gid = valid ? p.sorted[wk.z + t] : 0;
+      if (!LCB_IN(gid >= 0 && gid < g.npix, kSiteTcBwd1, gid)) { gid = 0; valid = false; }
       // A chunk whose boxes all lie off the map issued no MMA: its
       // accumulator holds a previous chunk's values and its gradient is zero.
       bool live = false;
@@ -1383,7 +1427,6 @@ __global__ void __launch_bounds__(kBwd1Threads, 1) tc_bwd1_kernel(const __grid_c
 constexpr int kB2Rows = 64;                       // K rows per stage
 constexpr int kBwd2Builders = 256;                // builder threads (warps 2..9)
 constexpr int kB2Groups = kBwd2Builders / kB2Rows;  // stage gs is built by group gs % 4
-constexpr int kBwd2MaxRanges = 8;                 // cell rows per item (rpi <= 16 / 2)
 constexpr int kBwd2Threads = 64 + kBwd2Builders + 128;  // MMA warp, TMA warp, builders, epilogue
 
 struct Bwd2Item {
@@ -1439,6 +1482,23 @@ __device__ __forceinline__ int2 item_range(const TcGeom& g, const int* __restric
   const int s0 = fine_off[row0 + (long long)it.ca * kColBins + la];
   const int s1 = fine_off[row0 + (long long)it.cb * kColBins + lb + 1];
   return make_int2(s0, max(s0, s1));
+}
+
+__device__ __forceinline__ int2 range_or_zero(const TcGeom& g, const int* __restrict__ fine_off,
+                                              const Bwd2Item& it, int k, int nr) {
+  return k < nr ? item_range(g, fine_off, it, k) : make_int2(0, 0);
+}
+
+// Stages (64 sorted rows each) of an item over its nr cell-row ranges; an
+// item without candidates still runs one all-zero stage.
+__device__ __forceinline__ int item_stages(const TcGeom& g, const int* __restrict__ fine_off,
+                                           const Bwd2Item& it, int nr) {
+  int total = 0;
+  for (int k = 0; k < nr; ++k) {
+    const int2 rg = item_range(g, fine_off, it, k);
+    total += (rg.y - rg.x + kB2Rows - 1) / kB2Rows;
+  }
+  return max(total, 1);
 }
 
 template <int RADIUS>
@@ -1545,21 +1605,16 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++ic) {
         const Bwd2Item item = decode_item(g, it, RADIUS);
         const int nr = item.empty ? 0 : item.rb - item.ra + 1;
-        int2 rgs[kBwd2MaxRanges];
-        int total_st = 0;
-#pragma unroll
-        for (int k = 0; k < kBwd2MaxRanges; ++k) {
-          rgs[k] = make_int2(0, 0);
-          if (k < nr) {
-            rgs[k] = item_range(g, p.offsets, item, k);
-            total_st += (rgs[k].y - rgs[k].x + kB2Rows - 1) / kB2Rows;
-          }
-        }
-        const int last = max(total_st, 1) - 1;
+        const int last = item_stages(g, p.offsets, item, nr) - 1;
         int k = 0, j = 0;
+        int2 rg = range_or_zero(g, p.offsets, item, 0, nr);
         for (int q = 0; q <= last && ok; ++q, ++gs) {
-          while (k < nr && j * kB2Rows >= rgs[k].y - rgs[k].x) { ++k; j = 0; }
-          const int row = (k < nr ? rgs[k].x : 0) + (j++) * kB2Rows;
+          while (k < nr && j * kB2Rows >= rg.y - rg.x) {
+            ++k;
+            j = 0;
+            rg = range_or_zero(g, p.offsets, item, k, nr);
+          }
+          const int row = rg.x + (j++) * kB2Rows;
           const int s = gs % NST;
           const uint32_t use = gs / NST;
           if (!tc::mbar_wait(empty + s, (use & 1) ^ 1, abort)) { ok = false; break; }
@@ -1591,28 +1646,23 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       const Bwd2Item item = decode_item(g, it, RADIUS);
       const int l = item.l;
       const int nr = item.empty ? 0 : item.rb - item.ra + 1;
-      int2 rgs[kBwd2MaxRanges];
-      int total_st = 0;
-#pragma unroll
-      for (int k = 0; k < kBwd2MaxRanges; ++k) {
-        rgs[k] = make_int2(0, 0);
-        if (k < nr) {
-          rgs[k] = item_range(g, p.offsets, item, k);
-          total_st += (rgs[k].y - rgs[k].x + kB2Rows - 1) / kB2Rows;
-        }
-      }
-      const int last = max(total_st, 1) - 1;
+      const int last = item_stages(g, p.offsets, item, nr) - 1;
       const int* sb_l = p.sbase + (long long)l * g.npix;
       const uint4* gsh_l = p.gsh + (long long)l * g.npix * (NG * NU);
       int k = 0, j = 0;  // range and stage within it of item stage q
+      int2 rg = range_or_zero(g, p.offsets, item, 0, nr);
       for (int q = 0; q <= last && ok; ++q, ++gs) {
-        while (k < nr && j * kB2Rows >= rgs[k].y - rgs[k].x) { ++k; j = 0; }
-        const int s0 = k < nr ? rgs[k].x : 0;
-        const int s1 = k < nr ? rgs[k].y : 0;
+        while (k < nr && j * kB2Rows >= rg.y - rg.x) {
+          ++k;
+          j = 0;
+          rg = range_or_zero(g, p.offsets, item, k, nr);
+        }
+        const int s0 = rg.x;
+        const int s1 = rg.y;
         const int jj0 = j++;
         if ((int)(gs % kB2Groups) != gb) continue;
         const int pos = s0 + jj0 * kB2Rows + t;
-        const bool valid = pos < s1;
+        const bool valid = pos < s1 && LCB_IN(pos >= 0 && pos < g.npix, kSiteTcBwd2, pos);
         int pk = 0;
         if (valid) pk = sb_l[pos];
         const int s = gs % NST;
@@ -1698,7 +1748,8 @@ __global__ void tc_unsort_kernel(const __half* __restrict__ scratch, const int* 
   const int b = blockIdx.z;
   if (pix >= g.HW) return;
   const long long gid = (long long)b * g.HW + pix;
-  const int idx = inv[gid];
+  int idx = inv[gid];
+  if (!LCB_IN(idx >= -1 && idx < g.npix, kSiteTcUnsort, idx)) idx = -1;
   const __half* src = scratch + ((long long)l * g.npix + (idx < 0 ? 0 : idx)) * g.RDP;
   __half* dst = out + ((long long)b * g.L + l) * g.RD2 * g.HW + pix;
   for (int d0 = 0; d0 < g.RD2; d0 += 8) {
@@ -1835,22 +1886,29 @@ bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStr
                                              W.work_count, ncells, g.ncell);
     count_launch();
     if (!check_launch("tc_scan_small")) return false;
-    tc_scatter_kernel<<<blocks, threads, 0, s>>>(W.keyrank, W.offsets, W.sorted, W.inv, g);
+  } else {
+    const int nsb = (ncells + kScanBlock - 1) / kScanBlock;
+    tc_cellscan_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, ncells);
     count_launch();
-    return check_launch("tc_scatter");
+    if (!check_launch("tc_cellscan")) return false;
+    tc_blockscan_kernel<<<1, 1024, 0, s>>>(W.bsum, nsb, W.offsets + (size_t)ncells * kColBins,
+                                           W.work_count);
+    count_launch();
+    if (!check_launch("tc_blockscan")) return false;
+    tc_cellwrite_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, W.offsets,
+                                                   W.work, ncells, g.ncell);
+    count_launch();
+    if (!check_launch("tc_cellwrite")) return false;
   }
-  const int nsb = (ncells + kScanBlock - 1) / kScanBlock;
-  tc_cellscan_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, ncells);
+  tc_scatter_kernel<<<blocks, threads, 0, s>>>(W.keyrank, W.offsets, W.sorted, W.inv, g);
   count_launch();
-  if (!check_launch("tc_cellscan")) return false;
-  tc_blockscan_kernel<<<1, 1024, 0, s>>>(W.bsum, nsb, W.offsets + (size_t)ncells * kColBins,
-                                         W.work_count);
+  if (!check_launch("tc_scatter")) return false;
+  if (!deterministic_mode()) return true;
+  const long long nbins = (long long)ncells * kColBins;
+  tc_rank_fix_kernel<<<(unsigned)((nbins * 32 + 255) / 256), 256, 0, s>>>(W.offsets, W.sorted,
+                                                                        W.keyrank, nbins, g.npix);
   count_launch();
-  if (!check_launch("tc_blockscan")) return false;
-  tc_cellwrite_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, W.offsets,
-                                                 W.work, ncells, g.ncell);
-  count_launch();
-  if (!check_launch("tc_cellwrite")) return false;
+  if (!check_launch("tc_rank_fix")) return false;
   tc_scatter_kernel<<<blocks, threads, 0, s>>>(W.keyrank, W.offsets, W.sorted, W.inv, g);
   count_launch();
   return check_launch("tc_scatter");
@@ -2220,6 +2278,8 @@ int tc_device_status(bool reset) {
   return v;
 }
 
+LCB_BOUNDS_READER(bounds_read_tc)
+
 }  // namespace lcb200
 
 // ---------------------------------------------------------------------------
@@ -2291,7 +2351,8 @@ extern "C" bool launchLocalCorrB200PyramidForwardNoAlloc(
   }
   void* ws = noalloc_scratch_ptr();
   if (!ws) return false;
-  return tc_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H1, W1, C, radius, levels,
-                    coords_dtype, ymajor, scale, nullptr, ws, LCB200_NOALLOC_SCRATCH_BYTES,
-                    stream);
+  return bounds_finish(tc_forward(fmap1, fmap2_packed, coords, corr, B, H1, W1, H1, W1, C,
+                                  radius, levels, coords_dtype, ymajor, scale, nullptr, ws,
+                                  LCB200_NOALLOC_SCRATCH_BYTES, stream),
+                       stream);
 }

@@ -335,7 +335,9 @@ spatial_fwd_tiled(const T* __restrict__ in1, const T* __restrict__ in2, T* __res
     for (int u = t; u < kFCK * F::TR2 * U2; u += 32 * RD) {
       const int ux = u % U2, row = (u / U2) % F::TR2, cc = u / (U2 * F::TR2);
       const int c = c0 + cc, gy = h0 - S::R + row, gx = w0 - S::R4 + 4 * ux;
-      const bool v = c < C && gy >= 0 && gy < H && gx >= 0 && gx < W;
+      const bool v = c < C && gy >= 0 && gy < H && gx >= 0 && gx < W &&
+                     LCB_IN(c * HW + (long long)gy * W + gx + 4 <= (long long)C * HW,
+                            kSiteSpatial, c * HW + (long long)gy * W + gx);
       cp4(s2 + buf * F::SL2 + (cc * F::TR2 + row) * F::S2 + 4 * ux,
           v ? i2b + c * HW + (long long)gy * W + gx : in2, v);
     }
@@ -433,7 +435,9 @@ spatial_bwd_tiled(const T* __restrict__ gout, const T* __restrict__ X, T* __rest
     for (int u = t; u < kBCK * Bt::XR * UX; u += 128) {
       const int ux = u % UX, row = (u / UX) % Bt::XR, cc = u / (UX * Bt::XR);
       const int c = c0 + cc, gy = h0 - S::R + row, gxx = w0 - S::R4 + 4 * ux;
-      const bool v = c < C && gy >= 0 && gy < H && gxx >= 0 && gxx < W;
+      const bool v = c < C && gy >= 0 && gy < H && gxx >= 0 && gxx < W &&
+                     LCB_IN(c * HW + (long long)gy * W + gxx + 4 <= (long long)C * HW,
+                            kSiteSpatial, c * HW + (long long)gy * W + gxx);
       cp4(Xs + (cc * Bt::XR + row) * Bt::SX + 4 * ux,
           v ? xb + c * HW + (long long)gy * W + gxx : X, v);
     }
@@ -623,5 +627,7 @@ bool spatial_backward(const void* in1, const void* in2, const void* g, void* g1,
       return false;
   }
 }
+
+LCB_BOUNDS_READER(bounds_read_spatial)
 
 }  // namespace lcb200

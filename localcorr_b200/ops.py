@@ -173,6 +173,36 @@ def _map_dims(fmap1, fmap2_packed, levels, map_hw):
     return h2, w2
 
 
+_USER_DETERMINISTIC = False
+_LIB_DETERMINISTIC = None  # the mode last pushed into the library
+
+
+def set_deterministic(on: bool) -> None:
+    """Deterministic mode of the library (``localCorrB200SetDeterministic``).
+
+    The tensor-core engine then sorts pixels in a fixed order and adds every
+    grad_fmap2 position once per call, so forward and backward give bitwise
+    identical results on identical inputs; a backward that would run on the
+    CUDA-core engine (scattered float atomics) raises instead. The mode is
+    also on while ``torch.use_deterministic_algorithms(True)`` is in effect.
+    """
+    global _USER_DETERMINISTIC
+    _USER_DETERMINISTIC = bool(on)
+    _sync_deterministic(_lib.require_library())
+
+
+def is_deterministic() -> bool:
+    return _USER_DETERMINISTIC or torch.are_deterministic_algorithms_enabled()
+
+
+def _sync_deterministic(lib) -> None:
+    global _LIB_DETERMINISTIC
+    want = is_deterministic()
+    if want != _LIB_DETERMINISTIC:
+        lib.localCorrB200SetDeterministic(int(want))
+        _LIB_DETERMINISTIC = want
+
+
 def _workspace(t: torch.Tensor, nbytes: int):
     if nbytes == 0:
         return None, 0
@@ -191,6 +221,7 @@ def pyramid_corr_forward(fmap1, fmap2_packed, coords, radius, levels, dilation=1
     receives the pixel sort for the backward of the same coords
     (``...ForwardKeepSort`` entry)."""
     lib = _lib.require_library()
+    _sync_deterministic(lib)
     b, h, w, c = fmap1.shape
     rd = 2 * radius + 1
     dt = _dtype_code(fmap1)
@@ -237,6 +268,7 @@ def pyramid_corr_backward(fmap1, fmap2_packed, coords, corr_grad, radius, levels
     ``sort_state``: the buffer a :func:`pyramid_corr_forward` of the same
     coords filled (``...BackwardWithSort`` entry: no second sort)."""
     lib = _lib.require_library()
+    _sync_deterministic(lib)
     b, h, w, c = fmap1.shape
     dt = _dtype_code(fmap1)
     cdt = _dtype_code(coords)

@@ -63,6 +63,26 @@ def test_version_and_error_getters(lib):
     assert lib.localCorrB200LaunchCount(0) >= 0
 
 
+def test_deterministic_mode_switch(lib):
+    import torch
+
+    import localcorr_b200 as lc
+
+    assert lib.localCorrB200GetDeterministic() == 0
+    lc.set_deterministic(True)
+    try:
+        assert lib.localCorrB200GetDeterministic() == 1 and lc.is_deterministic()
+    finally:
+        lc.set_deterministic(False)
+    assert lib.localCorrB200GetDeterministic() == 0
+    torch.use_deterministic_algorithms(True)
+    try:
+        assert lc.is_deterministic()
+    finally:
+        torch.use_deterministic_algorithms(False)
+    assert not lc.is_deterministic()
+
+
 def _fwd(lib, **kw):
     a = dict(B=1, H=16, W=16, C=8, r=2, L=3, dil=1, half=False, ymajor=False)
     a.update(kw)
@@ -146,3 +166,31 @@ def test_map_dims_prototypes_extend_the_plain_ones():
     bwd = _lib.PROTOTYPES["launchLocalCorrB200PyramidBackward"][1]
     bwd2 = _lib.PROTOTYPES["launchLocalCorrB200PyramidBackwardMapDims"][1]
     assert bwd2[:9] == bwd[:9] and bwd2[9:11] == [ctypes.c_int] * 2 and bwd2[11:] == bwd[9:]
+
+
+def test_bounds_checked_build_loads_by_environment(tmp_path):
+    """LOCALCORR_B200_BOUNDS_CHECK=1 selects liblocalcorr_b200_checked.so,
+    which exports the same symbols and counts violations (the normal build
+    reports -1)."""
+    import os
+    import subprocess
+    import sys
+
+    from localcorr_b200.csrc import build
+
+    build.build(bounds_check=True)
+    code = (
+        "from localcorr_b200 import _lib\n"
+        "lib = _lib.load_library()\n"
+        "assert lib is not None\n"
+        "print(_lib.LIB_PATH.name, lib.localCorrB200BoundsViolations(0))\n"
+    )
+    env = dict(os.environ, LOCALCORR_B200_BOUNDS_CHECK="1")
+    res = subprocess.run([sys.executable, "-c", code], cwd=ROOT, env=env, capture_output=True,
+                         text=True, timeout=300)
+    assert res.returncode == 0, res.stderr
+    assert res.stdout.split() == ["liblocalcorr_b200_checked.so", "0"]
+    assert _lib.load_library().localCorrB200BoundsViolations(0) == -1
+    raw = ctypes.CDLL(str(_lib.LIB_PATH_CHECKED))
+    for name in _declared_symbols():
+        assert hasattr(raw, name), f"{name} not exported by the checked build"

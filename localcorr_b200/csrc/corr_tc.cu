@@ -59,6 +59,9 @@ namespace {
 
 constexpr int kCellY = 8, kCellX = 16, kTile = 128;
 constexpr int kColBins = kCellX;  // sort bins per cell: the level-0 base column in the cell
+// Work counters of the persistent kernels' dynamic schedulers: [0] grad_fmap2
+// items; zeroed by the gradient-record kernel that precedes their user.
+constexpr int kWorkCounters = 4;
 constexpr int kMaxTcLevels = 4;
 constexpr int kBwd1Threads = 64 + 256 + 128;  // grad_fmap1: producer, MMA, 2 x 4 builder warps, 4 epilogue warps
 constexpr int kFwdEG = 3;          // forward epilogue warp groups
@@ -1002,7 +1005,9 @@ __global__ void __launch_bounds__(128)
 tc_gint_kernel(const __half* __restrict__ corr_grad, const void* __restrict__ coords,
                int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
                int* __restrict__ sbase, __half* __restrict__ grad_f1, int ymajor,
-               int vec_ok, int acc_f1, TcGeom g) {
+               int vec_ok, int acc_f1, int* __restrict__ wctr, TcGeom g) {
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0 && threadIdx.x < kWorkCounters)
+    wctr[threadIdx.x] = 0;
   using S = GintShape<RADIUS>;
   constexpr int RD = S::RD, SU = S::SU;
   extern __shared__ __align__(16) uint8_t gsm[];
@@ -1041,7 +1046,9 @@ __global__ void __launch_bounds__(128)
 tc_gint_tma_kernel(const __grid_constant__ CUtensorMap tmap_g, const void* __restrict__ coords,
                    int coords_f32, const int* __restrict__ inv, uint4* __restrict__ gsh,
                    int* __restrict__ sbase, __half* __restrict__ grad_f1,
-                   int ymajor, int acc_f1, int nblk, int nruns, TcGeom g) {
+                   int ymajor, int acc_f1, int nblk, int nruns, int* __restrict__ wctr,
+                   TcGeom g) {
+  if (blockIdx.x == 0 && threadIdx.x < kWorkCounters) wctr[threadIdx.x] = 0;
   using S = GintShape<RADIUS>;
   constexpr int RD = S::RD;
   constexpr int SU = S::SU;
@@ -1116,6 +1123,7 @@ struct alignas(64) TcBwdParams {
   int nstage;
   uint32_t stage_bytes;
   long long nitems;
+  int* item_next;  // grad_fmap2 item counter (zeroed by the gradient-record kernel)
   int nbg;     // grad_fmap1 builder groups (1 or 2)
   int acc_f1;  // add grad_fmap1 into the existing rows instead of overwriting them
   float scale; // output scale, applied to the float32 accumulators
@@ -1511,6 +1519,14 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   // stages of each item, written by the TMA producer before the item's first
   // stage is released (ring of 16 > the most items the producer can lead by)
   __shared__ int item_nst[16];
+  // Items are taken dynamically: the TMA producer takes the next item index
+  // from a global counter (coarse, long items first) and publishes it in a
+  // 16-slot ring with one mbarrier per slot; the MMA thread, the builders
+  // and the epilogue read the same sequence (-1 ends it). No role lags the
+  // producer by 16 items (at most the stage count plus the two accumulator
+  // buffers), so a slot is read by all before it is reused.
+  __shared__ int item_ring[16];
+  __shared__ __align__(8) uint64_t item_bar[16];
   const TcGeom& g = p.g;
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int NST = p.nstage;
@@ -1537,6 +1553,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     }
     for (int i = 0; i < 2; ++i) { tc::mbar_init(acc_full + i, 1); tc::mbar_init(acc_empty + i, kTile); }
     tc::mbar_init(fin_bar, 1);
+    for (int i = 0; i < 16; ++i) tc::mbar_init(item_bar + i, 1);
     tc::fence_mbar_init();
     abort_flag = 0;
   }
@@ -1566,7 +1583,9 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       const uint32_t stage_units = SB >> 4;
       const uint32_t idesc = tc::idesc_f16_f32(128, g.C, true, true);
       bool ok = true;
-      for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++ac) {
+      for (;; ++ac) {
+        if (!tc::mbar_wait(item_bar + (ac & 15), (ac >> 4) & 1, abort)) break;
+        if (item_ring[ac & 15] < 0) break;
         const int buf = ac & 1;
         if (!tc::mbar_wait(acc_empty + buf, ((ac >> 1) & 1) ^ 1, abort)) break;
         tc::tc_fence_after();
@@ -1602,7 +1621,11 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     if (lane == 0) {
       uint32_t gs = 0, ic = 0;
       bool ok = true;
-      for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x, ++ic) {
+      for (; ok; ++ic) {
+        const int it = atomicAdd(p.item_next, 1);
+        item_ring[ic & 15] = it < nitems ? it : -1;
+        tc::mbar_arrive(item_bar + (ic & 15));
+        if (it >= nitems) break;
         const Bwd2Item item = decode_item(g, it, RADIUS);
         const int nr = item.empty ? 0 : item.rb - item.ra + 1;
         const int last = item_stages(g, p.offsets, item, nr) - 1;
@@ -1642,7 +1665,10 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     const int t = bt % kB2Rows;
     uint32_t gs = 0;
     bool ok = true;
-    for (long long it = blockIdx.x; it < nitems && ok; it += gridDim.x) {
+    for (uint32_t ic = 0; ok; ++ic) {
+      if (!tc::mbar_wait(item_bar + (ic & 15), (ic >> 4) & 1, abort)) break;
+      const int it = item_ring[ic & 15];
+      if (it < 0) break;
       const Bwd2Item item = decode_item(g, it, RADIUS);
       const int l = item.l;
       const int nr = item.empty ? 0 : item.rb - item.ra + 1;
@@ -1700,7 +1726,10 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
     const int t = q * 32 + lane;   // D row = position in Q
     const uint32_t lane_addr = tmem + ((uint32_t)(q * 32) << 16);
     uint32_t ac = 0;
-    for (long long it = blockIdx.x; it < nitems; it += gridDim.x, ++ac) {
+    for (;; ++ac) {
+      if (!tc::mbar_wait(item_bar + (ac & 15), (ac >> 4) & 1, abort)) break;
+      const int it = item_ring[ac & 15];
+      if (it < 0) break;
       const int buf = ac & 1;
       if (!tc::mbar_wait(acc_full + buf, (ac >> 1) & 1, abort)) break;
       tc::tc_fence_after();
@@ -1793,7 +1822,7 @@ int num_sms() {
 // points put the sort state in a buffer of its own.
 struct WsLayout {
   size_t counts, offsets, keyrank, sorted, inv, work, work_count, cellpre, bsum, sbase, scratch,
-      gsh, f1s;
+      gsh, f1s, wctr;
   size_t sort_total;        // bytes of the sort state
   size_t fwd_total, total;  // bytes the forward / the backward need (both parts)
   long long max_work;
@@ -1817,6 +1846,7 @@ WsLayout ws_layout(const TcGeom& g) {
   w.cellpre = o; o = align256(o + ncells * 8);
   w.bsum = o; o = align256(o + (ncells + kScanBlock - 1) / kScanBlock * 8);
   w.sbase = o; o = align256(o + (size_t)g.L * g.npix * 4);
+  w.wctr = o; o = align256(o + kWorkCounters * 4);
   w.scratch = o; o = align256(o + (size_t)g.L * g.npix * g.RDP * 2);
   w.fwd_total = o;
   // the backward's records reuse the forward's output scratch
@@ -1840,6 +1870,7 @@ struct TcWs {
   __half* scratch;
   uint4* gsh;
   __half* f1s;
+  int* wctr;  // dynamic work counters (kWorkCounters)
 };
 
 // sort_ws: the sort state (or nullptr: it is the first sort_total bytes of
@@ -1864,6 +1895,7 @@ TcWs ws_pointers(void* sort_ws, void* ws, const WsLayout& L) {
   p.scratch = reinterpret_cast<__half*>(w + L.scratch);
   p.gsh = reinterpret_cast<uint4*>(w + L.gsh);
   p.f1s = reinterpret_cast<__half*>(w + L.f1s);
+  p.wctr = reinterpret_cast<int*>(w + L.wctr);
   return p;
 }
 
@@ -2135,7 +2167,7 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
     const int grid = std::min(nruns, num_sms() * per_sm);
     k0<<<grid, 128, smem0, s>>>(gmap, p1.coords, p1.coords_f32, inv, gsh,
                                 const_cast<int*>(p1.sbase), p1.grad_f1, ymajor, p1.acc_f1, nblk,
-                                nruns, g);
+                                nruns, p2.item_next, g);
   } else {
     dim3 ug((g.HW + 127) / 128, g.L, g.B);
     auto k0 = tc_gint_kernel<RADIUS>;
@@ -2143,7 +2175,7 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
     if (!ensure_smem_attr((const void*)k0, smem0)) return false;
     k0<<<ug, 128, smem0, s>>>(corr_grad, p1.coords, p1.coords_f32, inv, gsh,
                               const_cast<int*>(p1.sbase), p1.grad_f1, ymajor, vec_ok, p1.acc_f1,
-                              g);
+                              p2.item_next, g);
   }
   count_launch();
   if (!check_launch("tc_gint")) return false;
@@ -2252,6 +2284,7 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.scale = scale;
   p1.g = g;
   p1.nitems = (long long)B * g.items_before[levels];
+  p1.item_next = W.wctr;
   TcBwdParams p2 = p1;
   p1.nstage = n1 / 4;
   p1.nbg = n1 % 4;

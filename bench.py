@@ -690,7 +690,12 @@ def main(argv=None):
             traffic = None
             tf = ROOT / "profiles" / "traffic.json"
             if tf.exists():
-                traffic = json.loads(tf.read_text()).get(f"{args.config}:{kern}")
+                # bytes of one call at the capture's batch, scaled to this
+                # rank's images (independent work units)
+                tj = json.loads(tf.read_text())
+                traffic = tj.get(f"{args.config}:{kern}")
+                if traffic is not None and tj.get("batch"):
+                    traffic = traffic * cfg["B"] / tj["batch"]
             roof = {"bound": "hbm", "kernel": kern, "achieved": achieved, "peak": peak,
                     "peak_source": peak_kind, "unit": "GB/s", "frac": achieved / peak,
                     "traffic": traffic, "algorithmic_bytes": abytes,

@@ -68,6 +68,7 @@ bool bounds_read_tc(unsigned long long out[3], bool reset);
 bool bounds_read_simt(unsigned long long out[3], bool reset);
 bool bounds_read_spatial(unsigned long long out[3], bool reset);
 
+#ifdef LC_BOUNDS_CHECK
 namespace {
 std::atomic<long long> g_bounds_total{0};
 const char* const kSiteNames[kSiteCount] = {
@@ -87,6 +88,7 @@ const char* const kSiteNames[kSiteCount] = {
     "spatial (in2 element)",
 };
 }  // namespace
+#endif
 
 bool bounds_finish(bool ok, cudaStream_t s) {
 #ifdef LC_BOUNDS_CHECK

@@ -239,11 +239,12 @@ struct alignas(64) TcFwdParams {
 // ---------------------------------------------------------------------------
 // sort: histogram -> scan (+ work list) -> scatter
 // ---------------------------------------------------------------------------
+// Sort bin of pixel gid and its rank in the bin (atomic count), or key -1
+// when its windows miss every level.
 template <typename TC>
-__global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ counts,
-                               int2* __restrict__ keyrank, TcGeom g) {
-  const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
-  if (gid >= g.npix) return;
+__device__ __forceinline__ void hist_pixel(const TC* __restrict__ coords, int* __restrict__ counts,
+                                           int2* __restrict__ keyrank, const TcGeom& g,
+                                           long long gid) {
   const int b = (int)(gid / g.HW);
   const int p = (int)(gid - (long long)b * g.HW);
   const float cx = ldf(coords + (long long)b * 2 * g.HW + p);
@@ -262,6 +263,13 @@ __global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ 
   keyrank[gid] = kr;
 }
 
+template <typename TC>
+__global__ void tc_hist_kernel(const TC* __restrict__ coords, int* __restrict__ counts,
+                               int2* __restrict__ keyrank, TcGeom g) {
+  const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (gid < g.npix) hist_pixel(coords, counts, keyrank, g, gid);
+}
+
 // Scan of the sort bins, three passes over the cells (all blocks busy
 // instead of one): per-cell totals (pixels; 128-pixel chunks = work
 // entries) scanned within blocks of kScanBlock cells, the block totals
@@ -274,12 +282,13 @@ struct PairSum {
   __device__ int2 operator()(int2 a, int2 b) const { return make_int2(a.x + b.x, a.y + b.y); }
 };
 
+template <bool L2 = false>
 __device__ __forceinline__ void load_cell_bins(const int* __restrict__ counts, int i,
                                                int (&bins)[kColBins]) {
   const int4* src = reinterpret_cast<const int4*>(counts + (long long)i * kColBins);
 #pragma unroll
   for (int q = 0; q < kColBins / 4; ++q) {
-    const int4 v = src[q];
+    const int4 v = L2 ? __ldcg(src + q) : src[q];
     bins[4 * q] = v.x; bins[4 * q + 1] = v.y; bins[4 * q + 2] = v.z; bins[4 * q + 3] = v.w;
   }
 }
@@ -358,24 +367,44 @@ tc_cellwrite_kernel(const int* __restrict__ counts, const int2* __restrict__ cel
     work[coff + j] = make_int4(b, cell, off + j * kTile, min(kTile, cnt - j * kTile));
 }
 
-// The whole scan in one block of 1024 threads (up to kSmallScanCpt cells per
-// thread), for small problems (one or two images), where the three-pass
-// form's launches cost more than the scan itself.
+// Small problems (one or two images): the histogram and the whole scan in
+// one launch. Blocks of 1024 threads count their pixels; the last block to
+// finish (a ticket counter after a fence, no waiting) scans all the bins,
+// up to kSmallScanCpt cells per thread, where the three-pass form's
+// launches would cost more than the scan itself.
 constexpr int kSmallScanCpt = 4;
+template <typename TC>
 __global__ void __launch_bounds__(1024)
-tc_scan_small_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
-                     int4* __restrict__ work, int* __restrict__ total,
-                     int* __restrict__ work_count, int ncell_total, int ncell) {
+tc_hist_scan_kernel(const TC* __restrict__ coords, int* __restrict__ counts,
+                    int2* __restrict__ keyrank, int* __restrict__ done,
+                    int* __restrict__ offsets, int4* __restrict__ work, int* __restrict__ total,
+                    int* __restrict__ work_count, TcGeom g) {
   using Scan = cub::BlockScan<int2, 1024>;
   __shared__ typename Scan::TempStorage tmp;
-  const int c0 = threadIdx.x * kSmallScanCpt;
+  __shared__ int is_last;
+  const long long gid = blockIdx.x * (long long)blockDim.x + threadIdx.x;
+  if (gid < g.npix) hist_pixel(coords, counts, keyrank, g, gid);
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();  // this block's counts before its ticket
+    is_last = atomicAdd(done, 1) == (int)gridDim.x - 1;
+  }
+  __syncthreads();
+  if (!is_last) return;
+  __threadfence();  // every block's counts (read from L2 below)
+  const int ncell_total = g.B * g.ncell;
+  const int ncell = g.ncell;
+  // consecutive cells per thread: as few as the cell count allows (one
+  // cell per thread up to 1024 cells: whole 64-byte bin rows per lane)
+  const int cpt = (ncell_total + 1023) / 1024;
+  const int c0 = threadIdx.x * cpt;
   int2 mine = make_int2(0, 0);
 #pragma unroll
   for (int k = 0; k < kSmallScanCpt; ++k) {
     const int i = c0 + k;
-    if (i < ncell_total) {
+    if (k < cpt && i < ncell_total) {
       int bins[kColBins];
-      load_cell_bins(counts, i, bins);
+      load_cell_bins<true>(counts, i, bins);
       int cnt = 0;
 #pragma unroll
       for (int q = 0; q < kColBins; ++q) cnt += bins[q];
@@ -386,11 +415,11 @@ tc_scan_small_kernel(const int* __restrict__ counts, int* __restrict__ offsets,
   int2 ex, tot;
   Scan(tmp).ExclusiveScan(mine, ex, make_int2(0, 0), PairSum(), tot);
   int acc = ex.x, coff = ex.y;
-  for (int k = 0; k < kSmallScanCpt; ++k) {
+  for (int k = 0; k < cpt; ++k) {
     const int i = c0 + k;
     if (i >= ncell_total) break;
     int bins[kColBins];
-    load_cell_bins(counts, i, bins);
+    load_cell_bins<true>(counts, i, bins);
     const int off = acc;
     int4* dst = reinterpret_cast<int4*>(offsets + (long long)i * kColBins);
 #pragma unroll
@@ -1841,7 +1870,7 @@ WsLayout ws_layout(const TcGeom& g) {
   w.work = o; o = align256(o + (size_t)w.max_work * 16);
   w.work_count = o; o = align256(o + 4);
   w.sort_total = o;
-  w.counts = o; o = align256(o + ncells * kColBins * 4);
+  w.counts = o; o = align256(o + (ncells * kColBins + 1) * 4);
   w.keyrank = o; o = align256(o + (size_t)g.npix * 8);
   w.cellpre = o; o = align256(o + ncells * 8);
   w.bsum = o; o = align256(o + (ncells + kScanBlock - 1) / kScanBlock * 8);
@@ -1901,24 +1930,33 @@ TcWs ws_pointers(void* sort_ws, void* ws, const WsLayout& L) {
 
 // Counting sort of the pixels into anchor cells + the chunk work list.
 bool tc_sort(const TcWs& W, const TcGeom& g, const void* co, int cdtype, cudaStream_t s) {
-  if (cudaMemsetAsync(W.counts, 0, sizeof(int) * (size_t)g.B * g.ncell * kColBins, s) != cudaSuccess)
+  // the counts and, after them, the small path's block ticket
+  if (cudaMemsetAsync(W.counts, 0, sizeof(int) * ((size_t)g.B * g.ncell * kColBins + 1), s) !=
+      cudaSuccess)
     return check_launch("memset counts");
   const int threads = 256;
   const int blocks = (int)((g.npix + threads - 1) / threads);
-  if (cdtype == LCB200_F32)
-    tc_hist_kernel<float><<<blocks, threads, 0, s>>>((const float*)co, W.counts, W.keyrank, g);
-  else
-    tc_hist_kernel<__half><<<blocks, threads, 0, s>>>((const __half*)co, W.counts, W.keyrank, g);
-  count_launch();
-  if (!check_launch("tc_hist")) return false;
   const int ncells = g.B * g.ncell;
   if (ncells <= 1024 * kSmallScanCpt) {
-    tc_scan_small_kernel<<<1, 1024, 0, s>>>(W.counts, W.offsets,
-                                             W.work, W.offsets + (size_t)ncells * kColBins,
-                                             W.work_count, ncells, g.ncell);
+    const unsigned hb = (unsigned)((g.npix + 1023) / 1024);
+    int* done = W.counts + (size_t)ncells * kColBins;  // zeroed with the counts
+    int* total = W.offsets + (size_t)ncells * kColBins;
+    if (cdtype == LCB200_F32)
+      tc_hist_scan_kernel<float><<<hb, 1024, 0, s>>>((const float*)co, W.counts, W.keyrank, done,
+                                                      W.offsets, W.work, total, W.work_count, g);
+    else
+      tc_hist_scan_kernel<__half><<<hb, 1024, 0, s>>>((const __half*)co, W.counts, W.keyrank,
+                                                       done, W.offsets, W.work, total,
+                                                       W.work_count, g);
     count_launch();
-    if (!check_launch("tc_scan_small")) return false;
+    if (!check_launch("tc_hist_scan")) return false;
   } else {
+    if (cdtype == LCB200_F32)
+      tc_hist_kernel<float><<<blocks, threads, 0, s>>>((const float*)co, W.counts, W.keyrank, g);
+    else
+      tc_hist_kernel<__half><<<blocks, threads, 0, s>>>((const __half*)co, W.counts, W.keyrank, g);
+    count_launch();
+    if (!check_launch("tc_hist")) return false;
     const int nsb = (ncells + kScanBlock - 1) / kScanBlock;
     tc_cellscan_kernel<<<nsb, kScanBlock, 0, s>>>(W.counts, W.cellpre, W.bsum, ncells);
     count_launch();

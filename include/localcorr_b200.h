@@ -267,9 +267,13 @@ LCB200_API long long localCorrB200LaunchCount(int reset);
  * When on (process-wide, off by default), the tensor-core engine sorts the
  * pixels of a lookup in a fixed order (forward and backward) and adds every
  * grad_fmap2 position once per call, so repeated calls on the same inputs
- * give bitwise identical results; the CUDA-core engine's backward, whose
- * scattered float adds cannot be ordered, fails with an error instead.
- * Set it before the forward whose sort a ...BackwardWithSort reuses. */
+ * give bitwise identical results. The CUDA-core engine's backward then
+ * replaces its scattered float adds by a pull over the same sort (one writer
+ * per grad_fmap2 position, candidates in a fixed order); that needs
+ * dilation 1 and 1..4 levels, other configurations fail with an error, and
+ * its workspace (localCorrB200PyramidWorkspaceBytes* queried while the mode
+ * is on) is the sort's. Set it before the forward whose sort a
+ * ...BackwardWithSort reuses. */
 LCB200_API void localCorrB200SetDeterministic(int on);
 LCB200_API int localCorrB200GetDeterministic(void);
 

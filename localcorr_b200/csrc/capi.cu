@@ -3,6 +3,7 @@
 // error reporting around the kernels.
 #include <nvtx3/nvToolsExt.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -19,7 +20,13 @@ bool simt_forward(const void*, const void*, const void*, void*, int B, int H1, i
                   float scale, cudaStream_t);
 bool simt_backward(const void*, const void*, const void*, const void*, void*, float*, int B,
                    int H1, int W1, int H2, int W2, int C, int r, int levels, int dil, int dtype,
-                   int cdtype, bool ymajor, float scale, bool acc1, cudaStream_t);
+                   int cdtype, bool ymajor, float scale, bool acc1, bool add_f2, cudaStream_t);
+bool tc_det_pull_ok(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                    int dilation, std::string* why);
+size_t tc_det_pull_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels);
+bool tc_det_f2_pull(const void* f1, const void* co, const void* gout, float* f2g, int B, int H1,
+                    int W1, int H2, int W2, int C, int radius, int levels, int dtype, int cdtype,
+                    bool ymajor, float scale, void* ws, size_t ws_bytes, cudaStream_t s);
 bool tc_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
                  int dilation, int dtype, std::string* why);
 size_t tc_workspace_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
@@ -417,13 +424,34 @@ bool pyramid_backward_impl(const void* f1, const void* f2, const void* co, const
   }
   if (!ok) return false;
   if (deterministic_mode()) {
-    set_error("deterministic mode: the CUDA-core engine adds grad_fmap2 with float atomics; "
-              "only the tensor-core engine (float16 maps, dilation 1, 1..4 levels, C in "
-              "{64,128,192,256}, radius 3/4/8) has a deterministic backward");
-    return false;
+    // grad_fmap1 from the CUDA-core kernel without its scattered fmap2
+    // adds; grad_fmap2 pulled per output position over the sorted pixels
+    std::string why;
+    if (!tc_det_pull_ok(B, H1, W1, H2, W2, C, radius, levels, dil, &why)) {
+      set_error("deterministic mode: the CUDA-core backward's deterministic grad_fmap2 needs " +
+                why);
+      return false;
+    }
+    const size_t need = tc_det_pull_bytes(B, H1, W1, H2, W2, C, radius, levels);
+    if (!simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels, dil,
+                       dtype, cdtype, ymajor, scale, acc1, false, s))
+      return false;
+    if (lib_ws) {
+      ScratchLease lease(need, s);
+      if (!lease.ok()) return false;
+      return tc_det_f2_pull(f1, co, gout, f2g, B, H1, W1, H2, W2, C, radius, levels, dtype,
+                            cdtype, ymajor, scale, lease.ptr(), need, s);
+    }
+    if (ws_bytes < need || ws == nullptr) {
+      set_error("workspace too small: need " + std::to_string(need) + " B, got " +
+                std::to_string(ws_bytes));
+      return false;
+    }
+    return tc_det_f2_pull(f1, co, gout, f2g, B, H1, W1, H2, W2, C, radius, levels, dtype,
+                          cdtype, ymajor, scale, ws, ws_bytes, s);
   }
   return simt_backward(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels, dil,
-                       dtype, cdtype, ymajor, scale, acc1, s);
+                       dtype, cdtype, ymajor, scale, acc1, true, s);
 }
 
 bool pyramid_forward(const void* f1, const void* f2, const void* co, void* out, int B, int H1,
@@ -506,6 +534,12 @@ size_t localCorrB200PyramidWorkspaceBytesMapDims(int B, int H1, int W1, int H2, 
   ok = true;
   const bool b =
       use_tc(engine, B, H1, W1, H2, W2, C, radius, levels, dilation, dtype, &ok, true);
+  if (!b && deterministic_mode() &&
+      tc_det_pull_ok(B, H1, W1, H2, W2, C, radius, levels, dilation, nullptr)) {
+    // the CUDA-core backward's deterministic grad_fmap2 sorts the pixels
+    const size_t d = tc_det_pull_bytes(B, H1, W1, H2, W2, C, radius, levels);
+    return f ? std::max(d, tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, false)) : d;
+  }
   if (!f && !b) return 0;
   return tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, b);
 }

@@ -184,7 +184,7 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
                      const TC* __restrict__ coords, const T* __restrict__ corr_grad,
                      T* __restrict__ fmap1_grad, float* __restrict__ fmap2_grad,
                      int H1, int W1, int C, int r, int dil, bool ymajor,
-                     float scale, bool acc1, PyrGeom g) {
+                     float scale, bool acc1, bool add_f2, PyrGeom g) {
   constexpr int PG = kWarps * PPW;
   extern __shared__ float smem[];
   const int RD = 2 * r + 1;
@@ -278,9 +278,10 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
               const float4 v = ld4g(f2l + e);
               acc.x = fmaf(gk, v.x, acc.x); acc.y = fmaf(gk, v.y, acc.y);
               acc.z = fmaf(gk, v.z, acc.z); acc.w = fmaf(gk, v.w, acc.w);
-              asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(g2l + e),
-                           "f"(gk * f1v.x), "f"(gk * f1v.y), "f"(gk * f1v.z), "f"(gk * f1v.w)
-                           : "memory");
+              if (add_f2)
+                asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(g2l + e),
+                             "f"(gk * f1v.x), "f"(gk * f1v.y), "f"(gk * f1v.z), "f"(gk * f1v.w)
+                             : "memory");
             }
             float4* fg = reinterpret_cast<float4*>(f1gq + c);
             float4 o = *fg;
@@ -298,7 +299,7 @@ corr_bwd_simt_kernel(const T* __restrict__ fmap1, const T* __restrict__ fmap2p,
               const long long e = (rowoff + x) * C + c;
               if (!LCB_IN(e >= 0 && e < (long long)hl * wl * C, kSiteSimtBwd, e)) continue;
               acc = fmaf(gk, ldf(f2l + e), acc);
-              atomicAdd(g2l + e, gk * f1v);
+              if (add_f2) atomicAdd(g2l + e, gk * f1v);
             }
             f1gq[c] += acc;
           }
@@ -360,7 +361,7 @@ bool launch_fwd(const void* f1, const void* f2, const void* co, void* out, int B
 template <typename T, typename TC, int PPW>
 bool launch_bwd(const void* f1, const void* f2, const void* co, const void* gout,
                 void* f1g, float* f2g, int B, int H1, int W1, int C, int r, int dil,
-                bool ymajor, float scale, bool acc1, const PyrGeom& g, size_t smem,
+                bool ymajor, float scale, bool acc1, bool add_f2, const PyrGeom& g, size_t smem,
                 cudaStream_t s) {
   auto k = simt_v4(C, sizeof(T), {f1, f2, f2g}) ? corr_bwd_simt_kernel<T, TC, PPW, true>
                                                  : corr_bwd_simt_kernel<T, TC, PPW, false>;
@@ -368,7 +369,7 @@ bool launch_bwd(const void* f1, const void* f2, const void* co, const void* gout
   const int PG = kWarps * PPW;
   dim3 grid((H1 * W1 + PG - 1) / PG, B);
   k<<<grid, kThreads, smem, s>>>((const T*)f1, (const T*)f2, (const TC*)co, (const T*)gout,
-                                 (T*)f1g, f2g, H1, W1, C, r, dil, ymajor, scale, acc1, g);
+                                 (T*)f1g, f2g, H1, W1, C, r, dil, ymajor, scale, acc1, add_f2, g);
   count_launch();
   return check_launch("corr_bwd_simt");
 }
@@ -414,7 +415,7 @@ bool simt_forward(const void* f1, const void* f2, const void* co, void* out, int
 bool simt_backward(const void* f1, const void* f2, const void* co, const void* gout,
                    void* f1g, float* f2g, int B, int H1, int W1, int H2, int W2, int C,
                    int r, int levels, int dil, int dtype, int cdtype, bool ymajor, float scale,
-                   bool acc1, cudaStream_t s) {
+                   bool acc1, bool add_f2, cudaStream_t s) {
   const PyrGeom g = make_geom(H2, W2, C, levels);
   const int RD = 2 * r + 1;
   const int NX = (dil == 1) ? RD + 1 : 2 * RD;
@@ -432,9 +433,9 @@ bool simt_backward(const void* f1, const void* f2, const void* co, const void* g
   }
 #define LCB_BWD(T, TC)                                                                        \
   return ppw == 4 ? launch_bwd<T, TC, 4>(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, r, dil,    \
-                                         ymajor, scale, acc1, g, smem, s)                      \
+                                         ymajor, scale, acc1, add_f2, g, smem, s)              \
                   : launch_bwd<T, TC, 1>(f1, f2, co, gout, f1g, f2g, B, H1, W1, C, r, dil,    \
-                                         ymajor, scale, acc1, g, smem, s);
+                                         ymajor, scale, acc1, add_f2, g, smem, s);
   if (dtype == LCB200_F32) {
     if (cdtype == LCB200_F32) { LCB_BWD(float, float) }
     LCB_BWD(float, __half)

@@ -1798,6 +1798,74 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   if (threadIdx.x == 0 && abort_flag) atomicExch(&g_tc_status, 1);
 }
 
+// Deterministic grad_fmap2 of the CUDA-core engine (deterministic mode): the
+// pull of tc_bwd2_kernel on CUDA cores in float32, for maps of any dtype and
+// channel count. One block per output tile Q (8x16 level-l positions, one
+// item per tile in deterministic mode) and 32-channel slice; thread t owns
+// position t of Q and sums, over the tile's candidates in sorted order
+// (fixed in deterministic mode), G_p(q) * fmap1[p][c0 .. c0+31], where
+// G_p(q) is the pixel's scaled incoming gradient spread onto its (RD+1)^2
+// grid by the four-corner rule of corr_bwd_simt_kernel. Each position is
+// written by one thread, after the candidates in a fixed order.
+template <typename T, typename TC>
+__global__ void __launch_bounds__(128)
+det_f2_pull_kernel(const T* __restrict__ fmap1, const TC* __restrict__ coords,
+                   const T* __restrict__ corr_grad, const int* __restrict__ sorted,
+                   const int* __restrict__ offsets, float* __restrict__ grad_f2, int radius,
+                   int ymajor, float scale, TcGeom g) {
+  const int RD = 2 * radius + 1;
+  const Bwd2Item item = decode_item(g, blockIdx.x, radius);
+  const int c0 = blockIdx.y * 32;
+  const int nc = min(32, g.C - c0);
+  const int t = threadIdx.x;
+  const int l = item.l;
+  const int qy = item.qy0 + (t >> 4), qx = item.qx0 + (t & 15);
+  const bool inmap = !item.empty && qy < g.h[l] && qx < g.w[l];
+  const float inv = 1.f / (float)(1 << l);
+  const int nr = item.empty ? 0 : item.rb - item.ra + 1;
+  float acc[32];
+#pragma unroll
+  for (int c = 0; c < 32; ++c) acc[c] = 0.f;
+  const TC* cxb = coords + (long long)item.b * 2 * g.HW;
+  const T* gl = corr_grad + ((long long)item.b * g.L + l) * RD * RD * g.HW;
+  for (int k = 0; k < nr; ++k) {
+    const int2 rg = item_range(g, offsets, item, k);
+    for (int pos = rg.x; pos < rg.y; ++pos) {
+      const int gid = sorted[pos];
+      int pix = gid - item.b * g.HW;
+      if (!LCB_IN(pix >= 0 && pix < g.HW, kSiteTcBwd2, gid)) continue;
+      const float clx = ldf(cxb + pix) * inv, cly = ldf(cxb + g.HW + pix) * inv;
+      const float x0f = floorf(clx), y0f = floorf(cly);
+      const float dx = clx - x0f, dy = cly - y0f;
+      const int jx = qx - ((int)x0f - radius), jy = qy - ((int)y0f - radius);
+      float G = 0.f;
+      if (inmap && jx >= 0 && jx <= RD && jy >= 0 && jy <= RD) {
+        auto gv = [&](int iy, int ix) -> float {
+          if (iy < 0 || iy >= RD || ix < 0 || ix >= RD) return 0.f;
+          const int d = ymajor ? ix + RD * iy : iy + RD * ix;
+          return ldf(gl + (long long)d * g.HW + pix);
+        };
+        G = (gv(jy, jx) * ((1.f - dx) * (1.f - dy)) + gv(jy, jx - 1) * (dx * (1.f - dy)) +
+             gv(jy - 1, jx) * ((1.f - dx) * dy) + gv(jy - 1, jx - 1) * (dx * dy)) *
+            scale;
+      }
+      if (G != 0.f) {
+        const T* f1 = fmap1 + (long long)gid * g.C + c0;
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          if (c < nc) acc[c] = fmaf(G, ldf(f1 + c), acc[c]);
+      }
+    }
+  }
+  if (inmap) {
+    float* dst = grad_f2 + (long long)item.b * g.batch_elems + g.off[l] +
+                 ((long long)qy * g.w[l] + qx) * g.C + c0;
+#pragma unroll
+    for (int c = 0; c < 32; ++c)
+      if (c < nc) dst[c] += acc[c];
+  }
+}
+
 // scratch [L][npix][RDP] (sorted order) -> out [B][L][RD2][H][W]
 __global__ void tc_unsort_kernel(const __half* __restrict__ scratch, const int* __restrict__ inv,
                                  __half* __restrict__ out, TcGeom g) {
@@ -2061,6 +2129,62 @@ size_t tc_sort_state_bytes(int B, int H1, int W1, int H2, int W2, int C, int rad
   TcGeom g;
   if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, nullptr)) return 0;
   return ws_layout(g).sort_total;
+}
+
+// Deterministic CUDA-core grad_fmap2 (det_f2_pull_kernel): needs the pixel
+// sort, hence dilation 1, 1..4 levels and a radius whose anchor-cell
+// geometry exists. Workspace: the sort's buffers (everything the layout puts
+// before the forward scratch).
+bool tc_det_pull_ok(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+                    int dilation, std::string* why) {
+  if (dilation != 1) { if (why) *why = "dilation 1"; return false; }
+  if (levels < 1 || levels > kMaxTcLevels) { if (why) *why = "1..4 levels"; return false; }
+  TcGeom g;
+  std::string w;
+  if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, &w)) {
+    if (why) *why = w;
+    return false;
+  }
+  return true;
+}
+
+size_t tc_det_pull_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels) {
+  TcGeom g;
+  if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, nullptr)) return 0;
+  return ws_layout(g).scratch;
+}
+
+bool tc_det_f2_pull(const void* f1, const void* co, const void* gout, float* f2g, int B, int H1,
+                    int W1, int H2, int W2, int C, int radius, int levels, int dtype, int cdtype,
+                    bool ymajor, float scale, void* ws, size_t ws_bytes, cudaStream_t s) {
+  TcGeom g;
+  std::string why;
+  if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, &why)) {
+    set_error("deterministic backward: " + why);
+    return false;
+  }
+  const WsLayout L = ws_layout(g);
+  if (ws_bytes < L.scratch || ws == nullptr) {
+    set_error("deterministic backward: workspace too small");
+    return false;
+  }
+  TcWs W = ws_pointers(nullptr, ws, L);
+  if (!tc_sort(W, g, co, cdtype, s)) return false;
+  const dim3 grid((unsigned)((long long)B * g.items_before[levels]), (unsigned)((C + 31) / 32));
+#define LCB_PULL(T, TC)                                                                       \
+  det_f2_pull_kernel<T, TC><<<grid, 128, 0, s>>>((const T*)f1, (const TC*)co, (const T*)gout, \
+                                                 W.sorted, W.offsets, f2g, radius,            \
+                                                 ymajor ? 1 : 0, scale, g)
+  if (dtype == LCB200_F32) {
+    if (cdtype == LCB200_F32) LCB_PULL(float, float);
+    else LCB_PULL(float, __half);
+  } else {
+    if (cdtype == LCB200_F32) LCB_PULL(__half, float);
+    else LCB_PULL(__half, __half);
+  }
+#undef LCB_PULL
+  count_launch();
+  return check_launch("det_f2_pull");
 }
 
 // sort_ws == nullptr: ws holds the whole workspace (sort state first);

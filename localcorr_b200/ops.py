@@ -182,8 +182,9 @@ def set_deterministic(on: bool) -> None:
 
     The tensor-core engine then sorts pixels in a fixed order and adds every
     grad_fmap2 position once per call, so forward and backward give bitwise
-    identical results on identical inputs; a backward that would run on the
-    CUDA-core engine (scattered float atomics) raises instead. The mode is
+    identical results on identical inputs; the CUDA-core engine's backward
+    pulls grad_fmap2 over the same sort instead of scattering float atomics
+    (dilation 1 and 1..4 levels; other configurations raise). The mode is
     also on while ``torch.use_deterministic_algorithms(True)`` is in effect.
     """
     global _USER_DETERMINISTIC

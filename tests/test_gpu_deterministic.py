@@ -1,4 +1,4 @@
-"""Deterministic mode: bitwise-repeatable results from the tensor-core engine.
+"""Deterministic mode: bitwise-repeatable results from both engines.
 
 ``compute-sanitizer`` (racecheck) is closed on this pool, so races in the
 scattered grad_fmap2 reduction are caught the other way round: in
@@ -142,17 +142,59 @@ def test_block_training_step_repeats_bitwise():
         assert torch.equal(a[0], bb[0]) and torch.equal(a[1], bb[1])
 
 
-def test_cuda_core_backward_refuses_in_deterministic_mode():
-    b, c, h, w, levels, r = 1, 32, 16, 20, 2, 3
+@pytest.mark.parametrize("case", [(1, 32, 16, 20, 2, 3, torch.float32),
+                                  (2, 24, 23, 31, 4, 4, torch.float32),
+                                  (1, 33, 18, 26, 3, 4, torch.float16)],
+                         ids=lambda c: "b{}c{}_{}x{}_l{}r{}_{}".format(
+                             *c[:6], str(c[6]).split(".")[-1]))
+def test_cuda_core_backward_deterministic(case):
+    # float32 maps (or a channel count the tensor cores do not take): the
+    # CUDA-core backward without scattered atomics, grad_fmap2 pulled over
+    # the sorted pixels
+    b, c, h, w, levels, r, dt = case
     f1, f2 = oracle.make_fmaps(b, c, h, w, seed=61)
+    fm1 = ops.nchw_to_nhwc(f1.to(DEV, dt))
+    packed = ops.pyramid_build(f2.to(DEV, dt), levels)
+    co = oracle.make_coords_gauss_oob(b, h, w, 5.0, 0.1, seed=62).to(DEV, dt)
+    rd = 2 * r + 1
+    gout = torch.randn(b, levels, rd * rd, h, w,
+                       generator=torch.Generator().manual_seed(63)).to(DEV, dt)
+    s1, s2 = ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels, 1, False, 0.5)
+    lc.set_deterministic(True)
+    a1, a2 = ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels, 1, False, 0.5)
+    for _ in range(3):
+        x1, x2 = ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels, 1, False, 0.5)
+        assert torch.equal(a1, x1) and torch.equal(a2, x2)
+    tol = dict(rtol=1e-5, atol=1e-4) if dt == torch.float32 else F16TOL
+    torch.testing.assert_close(a1.float(), s1.float(), **tol)
+    torch.testing.assert_close(a2, s2, rtol=1e-5, atol=1e-4)
+    # accumulate flag: a second call adds into the same buffers
+    ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels, 1, False, 0.5, out=(x1, x2),
+                              accumulate=_lib.ACC_FMAP1 | _lib.ACC_FMAP2)
+    torch.testing.assert_close(x2, 2 * a2, rtol=1e-5, atol=1e-4)
+    xd1 = f1.double().requires_grad_(True)
+    xd2 = f2.double().requires_grad_(True)
+    if dt == torch.float16:
+        xd1 = f1.half().double().requires_grad_(True)
+        xd2 = f2.half().double().requires_grad_(True)
+    o = oracle.pyramid_corr(xd1, xd2, co.double().cpu(), levels, r) * 0.5
+    e1, e2 = torch.autograd.grad(o, [xd1, xd2], gout.double().cpu())
+    torch.testing.assert_close(a1.permute(0, 3, 1, 2).double().cpu(), e1, **tol)
+    g2n = ops.pyramid_build_backward(a2, (b, c, h, w), levels, torch.float32)
+    torch.testing.assert_close(g2n.double().cpu(), e2, **tol)
+
+
+def test_deterministic_mode_refuses_dilated_cuda_core_backward():
+    b, c, h, w, levels, r = 1, 16, 16, 20, 2, 2
+    f1, f2 = oracle.make_fmaps(b, c, h, w, seed=71)
     fm1 = ops.nchw_to_nhwc(f1.to(DEV))
     packed = ops.pyramid_build(f2.to(DEV), levels)
-    co = oracle.make_coords_uniform(b, h, w, 4.0, seed=62).to(DEV)
+    co = oracle.make_coords_uniform(b, h, w, 4.0, seed=72).to(DEV)
     gout = torch.ones(b, levels, (2 * r + 1) ** 2, h, w, device=DEV)
     lc.set_deterministic(True)
     # the forward has no scattered adds and still runs
-    ops.pyramid_corr_forward(fm1, packed, co, r, levels)
+    ops.pyramid_corr_forward(fm1, packed, co, r, levels, 2)
     with pytest.raises(RuntimeError, match="deterministic"):
-        ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels)
+        ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels, 2)
     lc.set_deterministic(False)
-    ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels)
+    ops.pyramid_corr_backward(fm1, packed, co, gout, r, levels, 2)

@@ -1526,8 +1526,8 @@ __device__ __forceinline__ int2 range_or_zero(const TcGeom& g, const int* __rest
   return k < nr ? item_range(g, fine_off, it, k) : make_int2(0, 0);
 }
 
-// Stages (64 sorted rows each) of an item over its nr cell-row ranges; an
-// item without candidates still runs one all-zero stage.
+// Stages (64 sorted rows each) of an item over its nr cell-row ranges (0
+// for an item without candidates: the producer skips it).
 __device__ __forceinline__ int item_stages(const TcGeom& g, const int* __restrict__ fine_off,
                                            const Bwd2Item& it, int nr) {
   int total = 0;
@@ -1535,7 +1535,7 @@ __device__ __forceinline__ int item_stages(const TcGeom& g, const int* __restric
     const int2 rg = item_range(g, fine_off, it, k);
     total += (rg.y - rg.x + kB2Rows - 1) / kB2Rows;
   }
-  return max(total, 1);
+  return total;
 }
 
 template <int RADIUS>
@@ -1644,20 +1644,29 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
   } else if (warp == 1) {
     // ---------------- TMA producer: B = 64-row tiles of sorted fmap1 ----------------
     // Same stage sequence as the builders: the item's ranges cut into 64-row
-    // stages (one all-zero stage for an item without candidates). Rows past
-    // a range's end belong to other cells (or are zero fill past the end);
+    // stages (items without candidates are never published). Rows past a
+    // range's end belong to other cells (or are zero fill past the end);
     // their A rows are zero.
     if (lane == 0) {
       uint32_t gs = 0, ic = 0;
       bool ok = true;
       for (; ok; ++ic) {
-        const int it = atomicAdd(p.item_next, 1);
+        // the next item with candidates (an item without any adds nothing:
+        // it is not published)
+        int it, nr = 0, nst = 0;
+        Bwd2Item item{};
+        for (;;) {
+          it = atomicAdd(p.item_next, 1);
+          if (it >= nitems) break;
+          item = decode_item(g, it, RADIUS);
+          nr = item.empty ? 0 : item.rb - item.ra + 1;
+          nst = item_stages(g, p.offsets, item, nr);
+          if (nst > 0) break;
+        }
         item_ring[ic & 15] = it < nitems ? it : -1;
         tc::mbar_arrive(item_bar + (ic & 15));
         if (it >= nitems) break;
-        const Bwd2Item item = decode_item(g, it, RADIUS);
-        const int nr = item.empty ? 0 : item.rb - item.ra + 1;
-        const int last = item_stages(g, p.offsets, item, nr) - 1;
+        const int last = nst - 1;
         int k = 0, j = 0;
         int2 rg = range_or_zero(g, p.offsets, item, 0, nr);
         for (int q = 0; q <= last && ok; ++q, ++gs) {

@@ -350,6 +350,35 @@ def run_step(cfg, f1, f2, coords, grads):
     return outs[-1], None
 
 
+def time_band_exchange(cfg, f2_band, steps, device, dist, world, rank):
+    """The row-band step's collective alone: the all-gather of the band
+    pyramids into the frame's pyramid (bands.gather_pyramid), timed with CUDA
+    events over `steps` exchanges after warm-up, max over ranks. Every rank
+    runs the same collectives in the same order."""
+    from localcorr_b200 import bands
+
+    b, c = f2_band.shape[0], f2_band.shape[1]
+    layout = bands.RowBandLayout(b, c, cfg["H"], cfg["W"], cfg["L"], world)
+    local = torch.ops.localcorr.pyramid_build(f2_band, cfg["L"])
+    for _ in range(3):
+        bands.gather_pyramid(layout, local, rank)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        bands.gather_pyramid(layout, local, rank)
+    end.record()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / steps
+    ms = max_over_ranks(ms / 1e3, dist, device) * 1e3
+    bytes_per_rank = layout.B * layout.max_band_elems * local.element_size()
+    return {"collective": "all_gather of the band pyramids (NCCL)", "ms_per_frame": ms,
+            "bytes_in_per_rank": bytes_per_rank * (world - 1),
+            "note": "timed alone after the step, same buffers; the step's time includes it"}
+
+
 def timed_loop(fn, steps, device):
     torch.cuda.synchronize(device)
     start = torch.cuda.Event(enable_timing=True)
@@ -667,6 +696,11 @@ def main(argv=None):
     barrier()
     e2e_elapsed = max_over_ranks(e2e_elapsed, dist, device)
 
+    exchange = None
+    if cfg.get("bands") and world > 1:
+        exchange = time_band_exchange(cfg, dev["f2"], max(args.steps, 10), device, dist, world,
+                                      rank)
+
     lookups_step = lookups_per_call(cfg) * cfg["iters"]
     shards = 1 if cfg.get("bands") else world  # row bands split one frame
     value = lookups_step * args.steps * shards / elapsed / 1e9
@@ -738,6 +772,8 @@ def main(argv=None):
             "cpu_baseline": cpu,
             "clocks": clocks,
         }
+        if exchange is not None:
+            line["exchange"] = exchange
         print(json.dumps(line), flush=True)
     # graphs go before the process group (none holds a collective, but a
     # graph that did would keep the exit waiting)

@@ -125,3 +125,41 @@ def test_no_alloc_rejects_levels_beyond_four(lib):
         _lib.F16, _lib.F16, False, 1.0, torch.cuda.current_stream().cuda_stream)
     assert not ok
     assert "levels must be in [1, 4]" in _lib.last_error(lib)
+
+
+def test_no_alloc_records_under_cuda_graph_capture(lib):
+    # After one call on the device (module loaded, kernel attributes set),
+    # the entry point can be recorded into a CUDA graph: it allocates
+    # nothing and makes no synchronising call. The replay reads the inputs'
+    # current contents.
+    lib.localCorrB200DeviceStatus(1)
+    radius, levels, scale = 4, 4, 1.0 / 16.0
+    fm1, packed, coords = _case(5)
+    b, h, w, c = fm1.shape
+    out = torch.empty((b, levels, 81, h, w), dtype=torch.float16, device=DEV)
+    ok, _ = _no_alloc(lib, fm1, packed, coords, radius, levels, scale)  # warm-up
+    assert ok, _lib.last_error(lib)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        with torch.cuda.graph(graph, stream=side):
+            ok = lib.launchLocalCorrB200PyramidForwardNoAlloc(
+                fm1.data_ptr(), packed.data_ptr(), coords.data_ptr(), out.data_ptr(), b, h, w,
+                c, radius, levels, _lib.F16, _lib.F16, False, scale,
+                torch.cuda.current_stream().cuda_stream)
+    assert ok, _lib.last_error(lib)
+    torch.cuda.current_stream().wait_stream(side)
+    for seed in (11, 23):
+        f2m, p2, co2 = _case(seed)
+        fm1.copy_(f2m)
+        packed.copy_(p2)
+        coords.copy_(co2)
+        graph.replay()
+        ref = ops.pyramid_corr_forward(fm1, packed, coords, radius, levels, 1, False, scale,
+                                       _lib.ENGINE_TC)
+        torch.cuda.synchronize()
+        torch.testing.assert_close(out.float(), ref.float(), rtol=1e-2, atol=1e-2)
+    del graph
+    assert lib.localCorrB200DeviceStatus(1) == 0

@@ -1875,9 +1875,17 @@ det_f2_pull_kernel(const T* __restrict__ fmap1, const TC* __restrict__ coords,
   }
 }
 
-// scratch [L][npix][RDP] (sorted order) -> out [B][L][RD2][H][W]
+// scratch [L][npix][RDP] (sorted order) -> out [B][L][RD2][H][W]. Each thread
+// moves one pixel's row: its 16-byte units are loaded in batches of up to 12,
+// all of a batch before any of its stores (the row sits at a random sorted
+// position, so the loads' latency is what bounds the kernel), then written
+// plane by plane (consecutive pixels -> coalesced stores).
+template <int RADIUS>
 __global__ void tc_unsort_kernel(const __half* __restrict__ scratch, const int* __restrict__ inv,
                                  __half* __restrict__ out, TcGeom g) {
+  constexpr int RD2 = (2 * RADIUS + 1) * (2 * RADIUS + 1);
+  constexpr int NL = (RD2 + 7) / 8;  // 16-byte units of a scratch row (RDP / 8)
+  constexpr int NB = NL < 12 ? NL : 12;
   const int pix = blockIdx.x * blockDim.x + threadIdx.x;
   const int l = blockIdx.y;
   const int b = blockIdx.z;
@@ -1885,15 +1893,25 @@ __global__ void tc_unsort_kernel(const __half* __restrict__ scratch, const int* 
   const long long gid = (long long)b * g.HW + pix;
   int idx = inv[gid];
   if (!LCB_IN(idx >= -1 && idx < g.npix, kSiteTcUnsort, idx)) idx = -1;
-  const __half* src = scratch + ((long long)l * g.npix + (idx < 0 ? 0 : idx)) * g.RDP;
-  __half* dst = out + ((long long)b * g.L + l) * g.RD2 * g.HW + pix;
-  for (int d0 = 0; d0 < g.RD2; d0 += 8) {
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (idx >= 0) v = *reinterpret_cast<const uint4*>(src + d0);
-    const __half* hv = reinterpret_cast<const __half*>(&v);
+  const __half* src = scratch + ((long long)l * g.npix + (idx < 0 ? 0 : idx)) * (NL * 8);
+  __half* dst = out + ((long long)b * g.L + l) * RD2 * g.HW + pix;
 #pragma unroll
-    for (int e = 0; e < 8; ++e)
-      if (d0 + e < g.RD2) dst[(long long)(d0 + e) * g.HW] = hv[e];
+  for (int k0 = 0; k0 < NL; k0 += NB) {
+    uint4 v[NB];
+#pragma unroll
+    for (int k = 0; k < NB; ++k)
+      v[k] = (idx >= 0 && 8 * (k0 + k) < g.RD2)
+                 ? *reinterpret_cast<const uint4*>(src + 8 * (k0 + k))
+                 : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int k = 0; k < NB; ++k) {
+      const int d0 = 8 * (k0 + k);
+      if (d0 >= g.RD2) break;
+      const __half* hv = reinterpret_cast<const __half*>(&v[k]);
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        if (d0 + e < g.RD2) dst[(long long)(d0 + e) * g.HW] = hv[e];
+    }
   }
 }
 
@@ -2267,7 +2285,12 @@ bool tc_forward(const void* f1, const void* f2, const void* co, void* out, int B
   }
   if (!ok) return false;
   dim3 ug((g.HW + 127) / 128, levels, B);
-  tc_unsort_kernel<<<ug, 128, 0, s>>>(scratch, inv, static_cast<__half*>(out), g);
+  __half* o = static_cast<__half*>(out);
+  switch (radius) {
+    case 3: tc_unsort_kernel<3><<<ug, 128, 0, s>>>(scratch, inv, o, g); break;
+    case 4: tc_unsort_kernel<4><<<ug, 128, 0, s>>>(scratch, inv, o, g); break;
+    default: tc_unsort_kernel<8><<<ug, 128, 0, s>>>(scratch, inv, o, g); break;
+  }
   count_launch();
   return check_launch("tc_unsort");
 }
@@ -2399,9 +2422,10 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   TcWs W = ws_pointers(sort_ws, ws, L);
   if (!sort_ws && !tc_sort(W, g, co, cdtype, s)) return false;
   {
+    // 8 warps per block, kGatherRows rows per warp
     const int rows_per_block = 8 * kGatherRows;
     const long long nb = (g.npix + rows_per_block - 1) / rows_per_block;
-    tc_gather_rows_kernel<<<(unsigned)nb, 32 * rows_per_block, 0, s>>>(
+    tc_gather_rows_kernel<<<(unsigned)nb, 256, 0, s>>>(
         static_cast<const __half*>(f1), W.sorted, W.offsets + (size_t)g.B * g.ncell * kColBins, W.f1s, g);
     count_launch();
     if (!check_launch("tc_gather_rows")) return false;

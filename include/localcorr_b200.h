@@ -261,6 +261,35 @@ LCB200_API int localCorrB200Version(void);
  * benchmarks). */
 LCB200_API long long localCorrB200LaunchCount(int reset);
 
+/* ---- Deferred grad_fmap2 for many lookups of one pair of maps -------------
+ * No reference counterpart (the reference runs one backward per lookup).
+ * A RAFT block runs many lookups against the same fmap1/fmap2. Instead of
+ * adding every lookup's grad_fmap2 into the float32 gradient pyramid (one
+ * read-modify-write of the whole pyramid per lookup), a training step can
+ * (1) per lookup, with the sort its ...ForwardKeepSort left, compute grad_fmap1
+ * and keep the lookup's grad_fmap2 records in a caller buffer of
+ * localCorrB200PyramidRecordsBytes(...) bytes, then (2) once, pull
+ * grad_fmap2 over all those lookups: every output tile sums the candidates
+ * of up to 12 lookups in one accumulator before one add. Tensor-core
+ * engine only (float16 maps, dilation 1); buffers 256-byte aligned.
+ * ...BackwardFmap1: workspace as for ...BackwardWithSort; accumulate:
+ * LCB200_ACC_FMAP1. ...BackwardFmap2Pull: sort_states[i] / records[i] are
+ * device pointers (a host array of nlookups each); workspace >= 256 bytes;
+ * accumulate: LCB200_ACC_FMAP2 adds into fmap2_grad_f32, else it is
+ * overwritten. The maps, scale and channel order are those of the lookups. */
+LCB200_API size_t localCorrB200PyramidRecordsBytes(int B, int H1, int W1, int H2, int W2, int C,
+                                                   int radius, int levels);
+LCB200_API bool launchLocalCorrB200PyramidBackwardFmap1(
+    const void* fmap1, const void* fmap2_packed, const void* coords, const void* corr_grad,
+    void* fmap1_grad, int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int coords_dtype, bool ymajor, float scale, int accumulate, const void* sort_state,
+    size_t sort_state_bytes, void* records, size_t records_bytes, void* workspace,
+    size_t workspace_bytes, cudaStream_t stream);
+LCB200_API bool launchLocalCorrB200PyramidBackwardFmap2Pull(
+    const void* const* sort_states, const void* const* records, int nlookups,
+    float* fmap2_grad_f32, int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    float scale, int accumulate, void* workspace, size_t workspace_bytes, cudaStream_t stream);
+
 /* ---- Deterministic mode ---------------------------------------------------
  * No reference counterpart (the reference's backward adds grad_fmap2 with
  * float atomics, cuda_pyramid/localcorr_cuda_pyramid_kernel.cu:909-916).

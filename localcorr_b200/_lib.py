@@ -110,6 +110,17 @@ PROTOTYPES = {
         _c_bool,
         [_c_void_p] * 5 + [_c_int] * 7 + [_c_float, _c_void_p],
     ),
+    "localCorrB200PyramidRecordsBytes": (_c_size_t, [_c_int] * 8),
+    "launchLocalCorrB200PyramidBackwardFmap1": (
+        _c_bool,
+        [_c_void_p] * 5 + [_c_int] * 9 + [_c_bool, _c_float, _c_int, _c_void_p, _c_size_t,
+                                          _c_void_p, _c_size_t, _c_void_p, _c_size_t, _c_void_p],
+    ),
+    "launchLocalCorrB200PyramidBackwardFmap2Pull": (
+        _c_bool,
+        [ctypes.POINTER(_c_void_p)] * 2 + [_c_int, _c_void_p] + [_c_int] * 8
+        + [_c_float, _c_int, _c_void_p, _c_size_t, _c_void_p],
+    ),
     "localCorrB200GetLastError": (ctypes.c_char_p, []),
     "localCorrB200DeviceStatus": (_c_int, [_c_int]),
     "localCorrB200Version": (_c_int, []),

@@ -39,6 +39,15 @@ bool tc_backward(const void*, const void*, const void*, const void*, void*, floa
                  bool ymajor, float scale, bool acc_f1, void* sort_ws, void*, size_t,
                  cudaStream_t);
 size_t tc_sort_state_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels);
+bool tc_backward_fmap1(const void* f1, const void* f2, const void* co, const void* gout,
+                       void* f1g, int B, int H1, int W1, int H2, int W2, int C, int radius,
+                       int levels, int cdtype, bool ymajor, float scale, bool acc_f1,
+                       void* sort_ws, void* ws, size_t ws_bytes, void* records,
+                       size_t records_bytes, cudaStream_t s);
+size_t tc_records_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels);
+bool tc_pull_lookups(const void* const* sort_states, const void* const* records, int n,
+                     float* f2g, int B, int H1, int W1, int H2, int W2, int C, int radius,
+                     int levels, float scale, void* ws, size_t ws_bytes, cudaStream_t s);
 bool tc_bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
                      int dilation, int dtype, std::string* why);
 int tc_device_status(bool reset);
@@ -578,6 +587,82 @@ bool launchLocalCorrB200PyramidBackwardWithSort(
                           H1, W1, H2, W2, C, radius, levels, dilation, dtype, coords_dtype,
                           ymajor, scale, accumulate, engine, workspace, workspace_bytes, false,
                           stream, sort_state, sort_state_bytes);
+}
+
+size_t localCorrB200PyramidRecordsBytes(int B, int H1, int W1, int H2, int W2, int C, int radius,
+                                        int levels) {
+  clear_error();
+  bool empty = false;
+  if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &empty) || empty)
+    return 0;
+  std::string why;
+  if (!tc_bwd_eligible(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &why)) return 0;
+  return tc_records_bytes(B, H1, W1, H2, W2, C, radius, levels);
+}
+
+bool launchLocalCorrB200PyramidBackwardFmap1(
+    const void* fmap1, const void* fmap2_packed, const void* coords, const void* corr_grad,
+    void* fmap1_grad, int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    int coords_dtype, bool ymajor, float scale, int accumulate, const void* sort_state,
+    size_t sort_state_bytes, void* records, size_t records_bytes, void* workspace,
+    size_t workspace_bytes, cudaStream_t stream) {
+  NvtxRange range("localcorr_b200 pyramid backward (grad_fmap1, records kept)");
+  clear_error();
+  bool empty = false;
+  if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &empty))
+    return false;
+  if (empty) return true;
+  if (coords_dtype != LCB200_F32 && coords_dtype != LCB200_F16) {
+    set_error("coords dtype must be LCB200_F32 (0) or LCB200_F16 (1)");
+    return false;
+  }
+  bool ok = true;
+  if (!use_tc(LCB200_ENGINE_TC, B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &ok, true,
+              fmap1, fmap2_packed))
+    return false;
+  const size_t sb = tc_sort_state_bytes(B, H1, W1, H2, W2, C, radius, levels);
+  if (!sort_state || sort_state_bytes < sb) {
+    set_error("sort state missing or too small: need " + std::to_string(sb) + " B");
+    return false;
+  }
+  const size_t need = tc_workspace_bytes(B, H1, W1, H2, W2, C, radius, levels, true) - sb;
+  if (workspace_bytes < need || (need && workspace == nullptr)) {
+    set_error("workspace too small: need " + std::to_string(need) + " B, got " +
+              std::to_string(workspace_bytes));
+    return false;
+  }
+  return bounds_finish(
+      tc_backward_fmap1(fmap1, fmap2_packed, coords, corr_grad, fmap1_grad, B, H1, W1, H2, W2,
+                        C, radius, levels, coords_dtype, ymajor, scale,
+                        (accumulate & LCB200_ACC_FMAP1) != 0, const_cast<void*>(sort_state),
+                        workspace, workspace_bytes, records, records_bytes, stream),
+      stream);
+}
+
+bool launchLocalCorrB200PyramidBackwardFmap2Pull(
+    const void* const* sort_states, const void* const* records, int nlookups,
+    float* fmap2_grad_f32, int B, int H1, int W1, int H2, int W2, int C, int radius, int levels,
+    float scale, int accumulate, void* workspace, size_t workspace_bytes, cudaStream_t stream) {
+  NvtxRange range("localcorr_b200 pyramid backward (grad_fmap2 of kept lookups)");
+  clear_error();
+  bool empty = false;
+  if (!validate_pyramid(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &empty))
+    return false;
+  if (empty) return true;
+  if (nlookups < 0 || (nlookups > 0 && (!sort_states || !records))) {
+    set_error("grad_fmap2 pull: nlookups sort states and records required");
+    return false;
+  }
+  if (!(accumulate & LCB200_ACC_FMAP2)) {
+    const PyrGeom g = make_geom(H2, W2, C, levels);
+    if (cudaMemsetAsync(fmap2_grad_f32, 0, sizeof(float) * (size_t)B * g.batch_elems, stream) !=
+        cudaSuccess)
+      return check_launch("memset fmap2_grad");
+  }
+  return bounds_finish(
+      tc_pull_lookups(sort_states, records, nlookups, fmap2_grad_f32, B, H1, W1, H2, W2, C,
+                      radius, levels, scale, workspace, workspace_bytes, stream),
+      stream);
 }
 
 size_t localCorrB200PyramidWorkspaceBytes(int B, int H1, int W1, int C, int radius, int levels,

@@ -1159,6 +1159,26 @@ struct alignas(64) TcBwdParams {
   TcGeom g;
 };
 
+// grad_fmap2 pull over one or more lookups of the same maps (a RAFT block's
+// iterations): each lookup brings its own sort, sorted fmap1 copy and
+// gradient records; an output tile sums the candidates of every lookup in
+// one accumulator and is added to the float32 gradient once.
+constexpr int kMaxPull = 12;
+struct alignas(64) TcPullParams {
+  CUtensorMap tmap_f1s[kMaxPull];  // per lookup: sorted fmap1 copy, 64-channel x 64-row boxes
+  const int* offsets[kMaxPull];    // per lookup: sort bin offsets
+  const uint4* gsh[kMaxPull];      // per lookup: pre-shifted gradient records
+  const int* sbase[kMaxPull];      // per lookup: packed level bases (sorted order)
+  int nlook;
+  float* grad_f2;
+  int nstage;
+  uint32_t stage_bytes;
+  long long nitems;
+  int* item_next;  // item counter, zero at launch
+  float scale;     // output scale, applied to the float32 accumulators
+  TcGeom g;
+};
+
 __device__ __forceinline__ void pixel_coords(const TcBwdParams& p, int b, int pix, float& cx,
                                              float& cy) {
   const TcGeom& g = p.g;
@@ -1538,8 +1558,21 @@ __device__ __forceinline__ int item_stages(const TcGeom& g, const int* __restric
   return total;
 }
 
+// Range kk (< nlook * nr) of an item over its lookups: lookup kk / nr, cell
+// row kk % nr; (0, 0) past the last.
+__device__ __forceinline__ int2 pull_range(const TcPullParams& p, const Bwd2Item& it, int kk,
+                                           int nr) {
+  return kk < nr * p.nlook ? item_range(p.g, p.offsets[kk / nr], it, kk % nr) : make_int2(0, 0);
+}
+
+__device__ __forceinline__ int pull_stages(const TcPullParams& p, const Bwd2Item& it, int nr) {
+  int total = 0;
+  for (int look = 0; look < p.nlook; ++look) total += item_stages(p.g, p.offsets[look], it, nr);
+  return total;
+}
+
 template <int RADIUS>
-__global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_constant__ TcBwdParams p) {
+__global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_constant__ TcPullParams p) {
   constexpr int RD = 2 * RADIUS + 1;
   constexpr int NG = RD + 1;
   constexpr int NU = (NG + 14) / 8;
@@ -1660,21 +1693,23 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           if (it >= nitems) break;
           item = decode_item(g, it, RADIUS);
           nr = item.empty ? 0 : item.rb - item.ra + 1;
-          nst = item_stages(g, p.offsets, item, nr);
+          nst = pull_stages(p, item, nr);
           if (nst > 0) break;
         }
         item_ring[ic & 15] = it < nitems ? it : -1;
         tc::mbar_arrive(item_bar + (ic & 15));
         if (it >= nitems) break;
         const int last = nst - 1;
+        const int nrt = nr * p.nlook;  // ranges over all lookups
         int k = 0, j = 0;
-        int2 rg = range_or_zero(g, p.offsets, item, 0, nr);
+        int2 rg = pull_range(p, item, 0, nr);
         for (int q = 0; q <= last && ok; ++q, ++gs) {
-          while (k < nr && j * kB2Rows >= rg.y - rg.x) {
+          while (k < nrt && j * kB2Rows >= rg.y - rg.x) {
             ++k;
             j = 0;
-            rg = range_or_zero(g, p.offsets, item, k, nr);
+            rg = pull_range(p, item, k, nr);
           }
+          const int look = min(k / nr, p.nlook - 1);
           const int row = rg.x + (j++) * kB2Rows;
           const int s = gs % NST;
           const uint32_t use = gs / NST;
@@ -1684,7 +1719,7 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
           tc::mbar_arrive_expect_tx(full + s, bbytes);
           uint8_t* sb = smem + (size_t)s * SB + 2 * kB2Rows * 128;
           for (int kc = 0; kc < g.KC; ++kc)
-            tc::tma_load_2d(sb + kc * kB2Rows * 128, &p.tmap_f1s, full + s, kc * 64, row);
+            tc::tma_load_2d(sb + kc * kB2Rows * 128, &p.tmap_f1s[look], full + s, kc * 64, row);
         }
       }
     }
@@ -1710,17 +1745,19 @@ __global__ void __launch_bounds__(kBwd2Threads, 1) tc_bwd2_kernel(const __grid_c
       const Bwd2Item item = decode_item(g, it, RADIUS);
       const int l = item.l;
       const int nr = item.empty ? 0 : item.rb - item.ra + 1;
-      const int last = item_stages(g, p.offsets, item, nr) - 1;
-      const int* sb_l = p.sbase + (long long)l * g.npix;
-      const uint4* gsh_l = p.gsh + (long long)l * g.npix * (NG * NU);
-      int k = 0, j = 0;  // range and stage within it of item stage q
-      int2 rg = range_or_zero(g, p.offsets, item, 0, nr);
+      const int last = pull_stages(p, item, nr) - 1;
+      const int nrt = nr * p.nlook;
+      int k = 0, j = 0;  // range (over all lookups) and stage within it of item stage q
+      int2 rg = pull_range(p, item, 0, nr);
       for (int q = 0; q <= last && ok; ++q, ++gs) {
-        while (k < nr && j * kB2Rows >= rg.y - rg.x) {
+        while (k < nrt && j * kB2Rows >= rg.y - rg.x) {
           ++k;
           j = 0;
-          rg = range_or_zero(g, p.offsets, item, k, nr);
+          rg = pull_range(p, item, k, nr);
         }
+        const int look = min(k / nr, p.nlook - 1);
+        const int* sb_l = p.sbase[look] + (long long)l * g.npix;
+        const uint4* gsh_l = p.gsh[look] + (long long)l * g.npix * (NG * NU);
         const int s0 = rg.x;
         const int s1 = rg.y;
         const int jj0 = j++;
@@ -2330,8 +2367,19 @@ bool bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, int 
 }
 
 template <int RADIUS>
-bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __half* corr_grad,
-                        const int* inv, uint4* gsh, float scale, int ymajor, cudaStream_t s) {
+bool launch_pull(const TcPullParams& p2, cudaStream_t s) {
+  const size_t smem2 = std::max<size_t>(bwd2_smem_bytes(p2.nstage, p2.stage_bytes), 120 * 1024);
+  auto k2 = tc_bwd2_kernel<RADIUS>;
+  if (!ensure_smem_attr((const void*)k2, smem2)) return false;
+  k2<<<num_sms(), kBwd2Threads, smem2, s>>>(p2);
+  count_launch();
+  return check_launch("tc_bwd2");
+}
+
+template <int RADIUS>
+bool launch_bwd_kernels(const TcBwdParams& p1, const TcPullParams& p2, const __half* corr_grad,
+                        const int* inv, uint4* gsh, float scale, int ymajor, bool pull,
+                        cudaStream_t s) {
   const TcGeom& g = p1.g;
   using GS = GintShape<RADIUS>;
   // 16-byte loads (and TMA rows) of the incoming gradient need HW % 8 == 0
@@ -2379,12 +2427,7 @@ bool launch_bwd_kernels(const TcBwdParams& p1, const TcBwdParams& p2, const __ha
   k1<<<num_sms(), 64 + 128 * p1.nbg + 128, smem1, s>>>(p1);
   count_launch();
   if (!check_launch("tc_bwd1")) return false;
-  const size_t smem2 = std::max<size_t>(bwd2_smem_bytes(p2.nstage, p2.stage_bytes), 120 * 1024);
-  auto k2 = tc_bwd2_kernel<RADIUS>;
-  if (!ensure_smem_attr((const void*)k2, smem2)) return false;
-  k2<<<num_sms(), kBwd2Threads, smem2, s>>>(p2);
-  count_launch();
-  return check_launch("tc_bwd2");
+  return pull ? launch_pull<RADIUS>(p2, s) : true;
 }
 
 }  // namespace
@@ -2398,10 +2441,29 @@ bool tc_bwd_eligible(int B, int H1, int W1, int H2, int W2, int C, int radius, i
 // sort_ws == nullptr: sort the coords into ws (single-buffer layout);
 // otherwise sort_ws holds the sort a forward made of the same coords and
 // geometry (tc_forward with that buffer) and ws holds the rest.
-bool tc_backward(const void* f1, const void* f2, const void* co, const void* gout, void* f1g,
-                 float* f2g, int B, int H1, int W1, int H2, int W2, int C, int radius,
-                 int levels, int cdtype, bool ymajor, float scale, bool acc_f1, void* sort_ws,
-                 void* ws, size_t ws_bytes, cudaStream_t s) {
+// A lookup's grad_fmap2 records kept for a later multi-lookup pull: the
+// sorted fmap1 copy, the packed level bases and the pre-shifted records.
+struct RecLayout {
+  size_t f1s, sbase, gsh, total;
+};
+RecLayout rec_layout(const TcGeom& g) {
+  RecLayout r{};
+  size_t o = 0;
+  r.f1s = o; o = align256(o + (size_t)g.npix * g.C * 2);
+  r.sbase = o; o = align256(o + (size_t)g.L * g.npix * 4);
+  r.gsh = o; o = align256(o + (size_t)g.L * g.npix * g.NG * g.NU * 16);
+  r.total = o;
+  return r;
+}
+
+// records == nullptr: the whole backward. Else grad_fmap1 only; the sorted
+// fmap1 copy, level bases and gradient records go to `records` for
+// tc_pull_lookups.
+bool tc_backward_impl(const void* f1, const void* f2, const void* co, const void* gout, void* f1g,
+                      float* f2g, int B, int H1, int W1, int H2, int W2, int C, int radius,
+                      int levels, int cdtype, bool ymajor, float scale, bool acc_f1, void* sort_ws,
+                      void* ws, size_t ws_bytes, void* records, size_t records_bytes,
+                      cudaStream_t s) {
   TcGeom g;
   int n1 = 0, n2 = 0;
   std::string why;
@@ -2420,6 +2482,17 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
     return false;
   }
   TcWs W = ws_pointers(sort_ws, ws, L);
+  if (records) {
+    const RecLayout R = rec_layout(g);
+    if (records_bytes < R.total || (reinterpret_cast<uintptr_t>(records) & 255)) {
+      set_error("tensor-core backward: records buffer too small or not 256-byte aligned");
+      return false;
+    }
+    uint8_t* rb = static_cast<uint8_t*>(records);
+    W.f1s = reinterpret_cast<__half*>(rb + R.f1s);
+    W.sbase = reinterpret_cast<int*>(rb + R.sbase);
+    W.gsh = reinterpret_cast<uint4*>(rb + R.gsh);
+  }
   if (!sort_ws && !tc_sort(W, g, co, cdtype, s)) return false;
   {
     // 8 warps per block, kGatherRows rows per warp
@@ -2480,20 +2553,132 @@ bool tc_backward(const void* f1, const void* f2, const void* co, const void* gou
   p1.g = g;
   p1.nitems = (long long)B * g.items_before[levels];
   p1.item_next = W.wctr;
-  TcBwdParams p2 = p1;
-  p1.nstage = n1 / 4;
-  p1.nbg = n1 % 4;
-  p2.nbg = 1;
-  p1.stage_bytes = (uint32_t)bwd1_stage_bytes(g);
+  TcPullParams p2;
+  memset(&p2, 0, sizeof(p2));
+  p2.tmap_f1s[0] = p1.tmap_f1s;
+  p2.offsets[0] = p1.offsets;
+  p2.gsh[0] = p1.gsh;
+  p2.sbase[0] = p1.sbase;
+  p2.nlook = 1;
+  p2.grad_f2 = f2g;
   p2.nstage = n2;
   p2.stage_bytes = (uint32_t)bwd2_stage_bytes(g);
+  p2.nitems = p1.nitems;
+  p2.item_next = p1.item_next;
+  p2.scale = scale;
+  p2.g = g;
+  p1.nstage = n1 / 4;
+  p1.nbg = n1 % 4;
+  p1.stage_bytes = (uint32_t)bwd1_stage_bytes(g);
   const __half* cg = static_cast<const __half*>(gout);
+  const bool pull = records == nullptr;
   switch (radius) {
-    case 3: return launch_bwd_kernels<3>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, s);
-    case 4: return launch_bwd_kernels<4>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, s);
-    case 8: return launch_bwd_kernels<8>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, s);
+    case 3: return launch_bwd_kernels<3>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, pull, s);
+    case 4: return launch_bwd_kernels<4>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, pull, s);
+    case 8: return launch_bwd_kernels<8>(p1, p2, cg, W.inv, W.gsh, scale, ymajor, pull, s);
     default: set_error("radius not instantiated"); return false;
   }
+}
+
+bool tc_backward(const void* f1, const void* f2, const void* co, const void* gout, void* f1g,
+                 float* f2g, int B, int H1, int W1, int H2, int W2, int C, int radius,
+                 int levels, int cdtype, bool ymajor, float scale, bool acc_f1, void* sort_ws,
+                 void* ws, size_t ws_bytes, cudaStream_t s) {
+  return tc_backward_impl(f1, f2, co, gout, f1g, f2g, B, H1, W1, H2, W2, C, radius, levels,
+                          cdtype, ymajor, scale, acc_f1, sort_ws, ws, ws_bytes, nullptr, 0, s);
+}
+
+bool tc_backward_fmap1(const void* f1, const void* f2, const void* co, const void* gout,
+                       void* f1g, int B, int H1, int W1, int H2, int W2, int C, int radius,
+                       int levels, int cdtype, bool ymajor, float scale, bool acc_f1,
+                       void* sort_ws, void* ws, size_t ws_bytes, void* records,
+                       size_t records_bytes, cudaStream_t s) {
+  if (!records) {
+    set_error("grad_fmap1 backward: records buffer required");
+    return false;
+  }
+  return tc_backward_impl(f1, f2, co, gout, f1g, nullptr, B, H1, W1, H2, W2, C, radius, levels,
+                          cdtype, ymajor, scale, acc_f1, sort_ws, ws, ws_bytes, records,
+                          records_bytes, s);
+}
+
+size_t tc_records_bytes(int B, int H1, int W1, int H2, int W2, int C, int radius, int levels) {
+  TcGeom g;
+  if (!make_tc_geom(B, H1, W1, H2, W2, C, radius, levels, &g, nullptr)) return 0;
+  return rec_layout(g).total;
+}
+
+// grad_fmap2 of n lookups of one pair of maps, from their kept sorts and
+// records: passes of up to kMaxPull lookups, each one grad_fmap2 kernel whose
+// output tiles sum every lookup's candidates before one add.
+bool tc_pull_lookups(const void* const* sort_states, const void* const* records, int n,
+                     float* f2g, int B, int H1, int W1, int H2, int W2, int C, int radius,
+                     int levels, float scale, void* ws, size_t ws_bytes, cudaStream_t s) {
+  TcGeom g;
+  int n1 = 0, n2 = 0;
+  std::string why;
+  if (!bwd_eligible(B, H1, W1, H2, W2, C, radius, levels, 1, LCB200_F16, &why, &g, &n1, &n2)) {
+    set_error("grad_fmap2 pull: " + why);
+    return false;
+  }
+  if (n <= 0) return true;
+  if (!ws || ws_bytes < 256 || (reinterpret_cast<uintptr_t>(ws) & 255)) {
+    set_error("grad_fmap2 pull: workspace of 256 aligned bytes required");
+    return false;
+  }
+  auto encode = get_encode_fn();
+  if (!encode) {
+    set_error("cuTensorMapEncodeTiled unavailable from the driver");
+    return false;
+  }
+  const WsLayout L = ws_layout(g);
+  const RecLayout R = rec_layout(g);
+  for (int i0 = 0; i0 < n; i0 += kMaxPull) {
+    const int m = std::min(kMaxPull, n - i0);
+    TcPullParams p;
+    memset(&p, 0, sizeof(p));
+    for (int j = 0; j < m; ++j) {
+      const uint8_t* st = static_cast<const uint8_t*>(sort_states[i0 + j]);
+      const uint8_t* rb = static_cast<const uint8_t*>(records[i0 + j]);
+      if (!st || !rb || ((reinterpret_cast<uintptr_t>(st) | reinterpret_cast<uintptr_t>(rb)) & 255)) {
+        set_error("grad_fmap2 pull: sort states and records must be 256-byte aligned buffers");
+        return false;
+      }
+      p.offsets[j] = reinterpret_cast<const int*>(st + L.offsets);
+      p.sbase[j] = reinterpret_cast<const int*>(rb + R.sbase);
+      p.gsh[j] = reinterpret_cast<const uint4*>(rb + R.gsh);
+      cuuint64_t dims[2] = {(cuuint64_t)C, (cuuint64_t)g.npix};
+      cuuint64_t strides[1] = {(cuuint64_t)C * 2};
+      cuuint32_t box[2] = {64, (cuuint32_t)kB2Rows};
+      cuuint32_t estr[2] = {1, 1};
+      CUresult r = encode(&p.tmap_f1s[j], CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                          const_cast<uint8_t*>(rb + R.f1s), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (r != CUDA_SUCCESS) {
+        set_error("cuTensorMapEncodeTiled failed for a kept sorted fmap1 copy");
+        return false;
+      }
+    }
+    p.nlook = m;
+    p.grad_f2 = f2g;
+    p.nstage = n2;
+    p.stage_bytes = (uint32_t)bwd2_stage_bytes(g);
+    p.nitems = (long long)B * g.items_before[levels];
+    p.item_next = static_cast<int*>(ws);
+    p.scale = scale;
+    p.g = g;
+    if (cudaMemsetAsync(ws, 0, sizeof(int), s) != cudaSuccess) return check_launch("memset");
+    bool ok = false;
+    switch (radius) {
+      case 3: ok = launch_pull<3>(p, s); break;
+      case 4: ok = launch_pull<4>(p, s); break;
+      case 8: ok = launch_pull<8>(p, s); break;
+      default: set_error("radius not instantiated"); return false;
+    }
+    if (!ok) return false;
+  }
+  return true;
 }
 
 int tc_device_status(bool reset) {

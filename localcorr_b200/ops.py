@@ -8,7 +8,9 @@ no CPU fallback.
 
 from __future__ import annotations
 
+import ctypes
 import math
+import os
 
 import torch
 
@@ -154,6 +156,58 @@ def sort_state_bytes(fmap1, fmap2_packed, radius, levels, dilation=1, engine=_li
     md = _map_dims(fmap1, fmap2_packed, levels, map_hw) or (h, w)
     return int(lib.localCorrB200PyramidSortStateBytes(b, h, w, md[0], md[1], c, radius, levels,
                                                       dilation, _dtype_code(fmap1), engine))
+
+
+def records_bytes(fmap1, fmap2_packed, radius, levels) -> int:
+    """Bytes of one lookup's kept grad_fmap2 records
+    (``localCorrB200PyramidRecordsBytes``; 0 when the tensor-core engine does
+    not take the configuration)."""
+    lib = _lib.require_library()
+    if fmap1.dtype != torch.float16:
+        return 0
+    b, h, w, c = fmap1.shape
+    return int(lib.localCorrB200PyramidRecordsBytes(b, h, w, h, w, c, radius, levels))
+
+
+def pyramid_corr_backward_fmap1(fmap1, fmap2_packed, coords, corr_grad, radius, levels, scale,
+                                g1, accumulate, sort_state, records):
+    """grad_fmap1 of one lookup into g1 (added when ``accumulate`` has
+    ``ACC_FMAP1``), its grad_fmap2 records left in ``records`` for
+    :func:`pyramid_corr_backward_fmap2_pull` (``...BackwardFmap1``)."""
+    lib = _lib.require_library()
+    _sync_deterministic(lib)
+    b, h, w, c = fmap1.shape
+    corr_grad = corr_grad.contiguous()
+    if corr_grad.dtype != fmap1.dtype:
+        corr_grad = corr_grad.to(fmap1.dtype)
+    nbytes = workspace_bytes(b, h, w, c, radius, levels, 1, _lib.F16, _lib.ENGINE_TC)
+    ws, nws = _workspace(fmap1, nbytes - sort_state.numel())
+    with torch.cuda.device(fmap1.device):
+        ok = _timed("pyramid_bwd", lambda: lib.launchLocalCorrB200PyramidBackwardFmap1(
+            fmap1.data_ptr(), fmap2_packed.data_ptr(), coords.data_ptr(), corr_grad.data_ptr(),
+            g1.data_ptr(), b, h, w, h, w, c, radius, levels, _dtype_code(coords), False,
+            float(scale), int(accumulate), sort_state.data_ptr(), sort_state.numel(),
+            records.data_ptr(), records.numel(), ws.data_ptr() if ws is not None else None, nws,
+            _stream(fmap1)))
+    _lib.check(ok, "pyramid correlation backward (grad_fmap1)", lib)
+
+
+def pyramid_corr_backward_fmap2_pull(fmap1, g2, radius, levels, scale, sort_states, records,
+                                     accumulate):
+    """grad_fmap2 of the kept lookups into the float32 packed g2 (added when
+    ``accumulate`` has ``ACC_FMAP2``) (``...BackwardFmap2Pull``)."""
+    lib = _lib.require_library()
+    b, h, w, c = fmap1.shape
+    n = len(sort_states)
+    arr = ctypes.c_void_p * max(n, 1)
+    sp = arr(*[t.data_ptr() for t in sort_states])
+    rp = arr(*[t.data_ptr() for t in records])
+    ws = torch.empty(256, dtype=torch.uint8, device=fmap1.device)
+    with torch.cuda.device(fmap1.device):
+        ok = _timed("pyramid_bwd_pull", lambda: lib.launchLocalCorrB200PyramidBackwardFmap2Pull(
+            sp, rp, n, g2.data_ptr(), b, h, w, h, w, c, radius, levels, float(scale),
+            int(accumulate), ws.data_ptr(), ws.numel(), _stream(fmap1)))
+    _lib.check(ok, "pyramid correlation backward (grad_fmap2 pull)", lib)
 
 
 def _map_dims(fmap1, fmap2_packed, levels, map_hw):
@@ -416,6 +470,12 @@ class ScaledPyramidCorr(torch.autograd.Function):
         return g1, g2, gc, None, None, None, None, None, None
 
 
+# A block's lookups defer their grad_fmap2 to one pull over all of them
+# (tensor-core engine); LOCALCORR_B200_DEFER_FMAP2=0 runs each lookup's
+# whole backward instead.
+DEFER_FMAP2 = os.environ.get("LOCALCORR_B200_DEFER_FMAP2", "1") not in ("0", "")
+
+
 class LookupGrads:
     """Gradient accumulators shared by the lookups of one pyramid block.
 
@@ -428,6 +488,9 @@ class LookupGrads:
     addition per lookup and map by a single pass at the end.
     """
 
+    # lookups whose grad_fmap2 is pulled in one pass (the kernel's limit)
+    MAX_PENDING = 12
+
     def __init__(self, fmap1_nhwc, fmap2_packed, fmap2_shape, levels):
         self.fmap1 = fmap1_nhwc
         self.fmap2_packed = fmap2_packed
@@ -435,15 +498,52 @@ class LookupGrads:
         self.levels = int(levels)
         self.g1 = None
         self.g2 = None
+        # lookups whose grad_fmap2 is deferred: (sort state, records) and the
+        # (radius, scale) they share
+        self.pending = []
+        self.pull_params = None
 
-    def buffers(self):
-        """(g1, g2, flags) for the next lookup's backward."""
+    def fmap1_buffer(self):
+        """(g1, flag) for the next lookup's grad_fmap1."""
         if self.g1 is None:
             self.g1 = torch.empty_like(self.fmap1)
+            return self.g1, 0
+        return self.g1, _lib.ACC_FMAP1
+
+    def fmap2_buffer(self):
+        """(g2, flag) for the next grad_fmap2 contribution."""
+        if self.g2 is None:
             self.g2 = torch.empty(self.fmap2_packed.shape, dtype=torch.float32,
                                   device=self.fmap1.device)
-            return self.g1, self.g2, 0
-        return self.g1, self.g2, _lib.ACC_FMAP1 | _lib.ACC_FMAP2
+            return self.g2, 0
+        return self.g2, _lib.ACC_FMAP2
+
+    def buffers(self):
+        """(g1, g2, flags) for the next lookup's whole backward."""
+        g1, f1 = self.fmap1_buffer()
+        g2, f2 = self.fmap2_buffer()
+        return g1, g2, f1 | f2
+
+    def defer(self, sort_state, records, radius, scale):
+        """Keep a lookup's grad_fmap2 records for one pull over many lookups."""
+        if self.pull_params not in (None, (radius, scale)):
+            self.flush()
+        self.pull_params = (radius, scale)
+        self.pending.append((sort_state, records))
+        if len(self.pending) >= self.MAX_PENDING:
+            self.flush()
+
+    def flush(self):
+        """grad_fmap2 of the deferred lookups, added into g2 in one pass."""
+        if not self.pending:
+            return
+        radius, scale = self.pull_params
+        g2, flag = self.fmap2_buffer()
+        pyramid_corr_backward_fmap2_pull(self.fmap1, g2, radius, self.levels, scale,
+                                         [p[0] for p in self.pending],
+                                         [p[1] for p in self.pending], flag)
+        self.pending = []
+        self.pull_params = None
 
 
 class LookupGradSink(torch.autograd.Function):
@@ -464,6 +564,7 @@ class LookupGradSink(torch.autograd.Function):
     @staticmethod
     def backward(ctx, _):
         st = ctx.state
+        st.flush()
         g1 = g2 = None
         if st.g1 is not None:
             if ctx.needs_input_grad[0]:
@@ -497,10 +598,21 @@ class PyramidLookup(torch.autograd.Function):
         (coords,) = ctx.saved_tensors
         st = ctx.state
         radius, levels, scale = ctx.params
-        g1, g2, flags = st.buffers()
-        pyramid_corr_backward(st.fmap1, st.fmap2_packed, coords, corr_grad, radius, levels,
-                              1, False, scale, out=(g1, g2), accumulate=flags,
-                              sort_state=ctx.sort_state)
+        nrec = (records_bytes(st.fmap1, st.fmap2_packed, radius, levels)
+                if ctx.sort_state is not None and DEFER_FMAP2 else 0)
+        if nrec:
+            # grad_fmap1 now; grad_fmap2 with the block's other lookups in
+            # one pass when the sink runs (or when MAX_PENDING have gathered)
+            g1, flag = st.fmap1_buffer()
+            records = torch.empty(nrec, dtype=torch.uint8, device=coords.device)
+            pyramid_corr_backward_fmap1(st.fmap1, st.fmap2_packed, coords, corr_grad, radius,
+                                        levels, scale, g1, flag, ctx.sort_state, records)
+            st.defer(ctx.sort_state, records, radius, scale)
+        else:
+            g1, g2, flags = st.buffers()
+            pyramid_corr_backward(st.fmap1, st.fmap2_packed, coords, corr_grad, radius, levels,
+                                  1, False, scale, out=(g1, g2), accumulate=flags,
+                                  sort_state=ctx.sort_state)
         ctx.sort_state = None
         gc = torch.zeros_like(coords) if ctx.needs_input_grad[1] else None
         return corr_grad.new_zeros(()), gc, None, None, None, None

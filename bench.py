@@ -151,6 +151,15 @@ def algorithmic_bytes(cfg, kernel):
     fwd = f1 + pyr + coords + out
     if kernel == "pyramid_fwd":
         return fwd
+    if kernel == "pyramid_bwd_fmap1":
+        # grad_fmap1 with the grad_fmap2 records kept: reads f1, pyramid,
+        # coords, corr_grad; writes grad_f1
+        return fwd + f1
+    if kernel == "pyramid_bwd_pull":
+        # grad_fmap2 of a block's lookups (up to 12 per call): their f1,
+        # coords and corr_grad in, the float32 grad pyramid out once
+        n = min(cfg["iters"], 12)
+        return f1 + n * (coords + out) + pyr * (4 // es)
     # backward: reads f1, pyramid, coords, corr_grad; writes grad_f1 and the
     # float32 grad pyramid (the C ABI's accumulator).
     return fwd + f1 + pyr * (4 // es)
@@ -719,7 +728,10 @@ def main(argv=None):
                 abytes = sum(nbs) / len(nbs)
                 achieved = sum(nbs) / sum(per[kern]) / 1e9
             else:
-                abytes = algorithmic_bytes(cfg, kern)
+                # with the deferred grad_fmap2 pull, a lookup's backward call
+                # computes grad_fmap1 only
+                deferred = kern == "pyramid_bwd" and "pyramid_bwd_pull" in per
+                abytes = algorithmic_bytes(cfg, "pyramid_bwd_fmap1" if deferred else kern)
                 achieved = abytes / dur / 1e9
             traffic = None
             tf = ROOT / "profiles" / "traffic.json"
@@ -727,7 +739,9 @@ def main(argv=None):
                 # bytes of one call at the capture's batch, scaled to this
                 # rank's images (independent work units)
                 tj = json.loads(tf.read_text())
-                traffic = tj.get(f"{args.config}:{kern}")
+                tkey = ("pyramid_bwd_fmap1" if kern == "pyramid_bwd" and "pyramid_bwd_pull" in per
+                        else kern)
+                traffic = tj.get(f"{args.config}:{tkey}")
                 if traffic is not None and tj.get("batch"):
                     traffic = traffic * cfg["B"] / tj["batch"]
             roof = {"bound": "hbm", "kernel": kern, "achieved": achieved, "peak": peak,

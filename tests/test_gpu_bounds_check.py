@@ -159,3 +159,36 @@ def test_keep_sort_and_deterministic_paths_checked(libs):
         checked.localCorrB200SetDeterministic(0)
     for x, y in zip(n, k):
         assert torch.equal(x, y)
+
+
+def test_deferred_fmap2_pull_checked(libs):
+    # grad_fmap1 with kept records for 3 lookups, then one grad_fmap2 pull
+    b, c, h, w, levels, r = 2, 128, 30, 44, 4, 4
+    f1, f2 = oracle.make_fmaps(b, c, h, w, seed=12)
+    fm1 = ops.nchw_to_nhwc(f1.to(DEV).half())
+    packed = ops.pyramid_build(f2.to(DEV).half(), levels)
+    cos = [_coords(kind, b, h, w, seed=13 + i).to(DEV, torch.float16)
+           for i, kind in enumerate(("oob", "far", "converge"))]
+    g = torch.Generator().manual_seed(14)
+    gouts = [torch.randn(b, levels, 81, h, w, generator=g).to(DEV, torch.float16) for _ in cos]
+
+    def run():
+        g1 = torch.empty_like(fm1)
+        g2 = torch.empty(packed.shape, dtype=torch.float32, device=DEV)
+        states, recs = [], []
+        for i, (co, go) in enumerate(zip(cos, gouts)):
+            st = torch.empty(ops.sort_state_bytes(fm1, packed, r, levels), dtype=torch.uint8,
+                             device=DEV)
+            ops.pyramid_corr_forward(fm1, packed, co, r, levels, scale=0.5, sort_state=st)
+            rec = torch.empty(ops.records_bytes(fm1, packed, r, levels), dtype=torch.uint8,
+                              device=DEV)
+            ops.pyramid_corr_backward_fmap1(fm1, packed, co, go, r, levels, 0.5, g1,
+                                            _lib.ACC_FMAP1 if i else 0, st, rec)
+            states.append(st)
+            recs.append(rec)
+        ops.pyramid_corr_backward_fmap2_pull(fm1, g2, r, levels, 0.5, states, recs, 0)
+        return g1.float(), g2
+
+    n, k = _run_both(libs, run)
+    for x, y in zip(n, k):
+        torch.testing.assert_close(y, x, rtol=1e-3, atol=1e-3)

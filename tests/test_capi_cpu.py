@@ -194,3 +194,25 @@ def test_bounds_checked_build_loads_by_environment(tmp_path):
     raw = ctypes.CDLL(str(_lib.LIB_PATH_CHECKED))
     for name in _declared_symbols():
         assert hasattr(raw, name), f"{name} not exported by the checked build"
+
+
+def test_deferred_fmap2_entry_points_validate_before_any_cuda_call(lib):
+    import ctypes as ct
+
+    # a pull over lookups needs their sort states and records
+    ok = lib.launchLocalCorrB200PyramidBackwardFmap2Pull(
+        None, None, 3, None, 1, 16, 16, 16, 16, 64, 4, 2, 0.125, 0, None, 0, None)
+    assert ok is False
+    assert "sort states and records" in _lib.last_error(lib)
+    # empty problems are successful no-ops, as for the other launchers
+    arr = (ct.c_void_p * 1)(None)
+    assert lib.launchLocalCorrB200PyramidBackwardFmap2Pull(
+        arr, arr, 0, None, 0, 16, 16, 16, 16, 64, 4, 2, 0.125, 0, None, 0, None) is True
+    # the grad_fmap1 call takes float16 maps and coords of dtype 0 or 1 only
+    ok = lib.launchLocalCorrB200PyramidBackwardFmap1(
+        None, None, None, None, None, 1, 16, 16, 16, 16, 64, 4, 2, 7, False, 0.125, 0,
+        None, 0, None, 0, None, 0, None)
+    assert ok is False
+    assert "coords dtype" in _lib.last_error(lib)
+    # an invalid configuration has no records
+    assert lib.localCorrB200PyramidRecordsBytes(1, 16, 16, 16, 16, 64, 4, 0) == 0

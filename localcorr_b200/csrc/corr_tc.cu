@@ -1541,11 +1541,6 @@ __device__ __forceinline__ int2 item_range(const TcGeom& g, const int* __restric
   return make_int2(s0, max(s0, s1));
 }
 
-__device__ __forceinline__ int2 range_or_zero(const TcGeom& g, const int* __restrict__ fine_off,
-                                              const Bwd2Item& it, int k, int nr) {
-  return k < nr ? item_range(g, fine_off, it, k) : make_int2(0, 0);
-}
-
 // Stages (64 sorted rows each) of an item over its nr cell-row ranges (0
 // for an item without candidates: the producer skips it).
 __device__ __forceinline__ int item_stages(const TcGeom& g, const int* __restrict__ fine_off,
